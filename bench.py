@@ -1,0 +1,457 @@
+#!/usr/bin/env python
+"""Benchmark of the paged decode path (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                  [--impl ours|reference] [--cpu-baseline-seconds S]
+
+A step is one decode-attention pass over one batch of the workload (for
+``tp70b``: decode of the rank's KV heads -> o_proj partial -> NCCL all-reduce).
+
+Workloads: ``gqa_b16`` (default, config 2), ``mha_b1``
+(config 1), ``gqa_long`` (config 3), ``tp70b`` (config 4).  At N > 1 the
+replicated workloads shard whole sequences across ranks (every rank decodes
+its own batch, no collective, "scaling": "weak"); ``tp70b`` shards KV heads
+and all-reduces the fp16 o_proj partials over NCCL ("scaling": "strong").
+
+value      tokens/s of the whole job with inputs resident in HBM, the steps
+           replayed from CUDA graphs, timed with CUDA events (max over ranks);
+           several input sets rotate so each step reads more than the 126 MB L2.
+e2e        the same metric through the public API (torch.ops.b200kv.*) with
+           pinned host buffers: every step copies q, the new K/V rows, slots,
+           block table and lengths host->device, appends the new token,
+           decodes, and copies the output back.
+roofline   achieved = algorithmic bytes per launch / mean CUDA-event duration
+           of the decode kernel; peak = measured HBM copy bandwidth
+           (MEASURED_PEAKS.json); traffic = DRAM bytes per launch from the
+           committed ncu summary of this kernel and workload, if present.
+cpu_baseline  the oracle (reference CPU eager path: paged gather + torch CPU
+           SDPA in fp32) on the host cores, bounded sample.
+--impl reference  times that CPU path alone on the same config (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode tokens/s (KV-stream HBM GB/s and % of peak in roofline)"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 2**20
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=None)
+    p.add_argument("--warmup", type=int, default=None)
+    p.add_argument("--workload", default="gqa_b16", choices=["gqa_b16", "mha_b1", "gqa_long", "tp70b"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--cpu-baseline-seconds", type=float, default=10.0)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+DEFAULT_STEPS = {"gqa_b16": 20000, "mha_b1": 20000, "gqa_long": 4000, "tp70b": 2000}
+
+
+# ----------------------------------------------------------- distributed ----
+def dist_setup(n):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- clocks ----
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ peaks ----
+def hbm_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from the committed ncu summary, if there is one."""
+    p = REPO / "profiles" / f"{kernel}_{workload}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*[=:]\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+# ------------------------------------------------------------- CPU oracle ----
+def cpu_oracle_rate(inp, budget_s: float, max_steps: int | None = None):
+    """Sequences/s of the oracle on a bounded sample (whole sequences, cycling)."""
+    from oracle import paged_attention as opa
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu = {k: getattr(inp, k).cpu() for k in ("q", "k_pool", "v_pool", "block_table", "context_lens")}
+    B = len(inp.ctx)
+    done, t0, b = 0, time.perf_counter(), 0
+    while True:
+        sl = slice(b, b + 1)
+        opa.decode_attention_cpu(cpu["q"][sl], cpu["k_pool"], cpu["v_pool"], cpu["block_table"][sl],
+                                 cpu["context_lens"][sl])
+        done += 1
+        b = (b + 1) % B
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_steps and done >= max_steps):
+            return done / el, done, el
+
+
+# ----------------------------------------------------------------- ours -----
+def build_inputs(cfg, rank, world, n_sets, device, start=0):
+    from torch_spyre_b200.workloads import make_decode_inputs
+
+    sets = []
+    for i in range(start, start + n_sets):
+        if cfg.name == "tp70b":
+            hkv = cfg.num_kv_heads // world
+            sets.append(make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}", num_kv_heads=hkv,
+                                           ctx=None))
+        else:
+            sets.append(make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}"))
+    return sets
+
+
+def run_ours(args, rank, world, local):
+    import torch_spyre_b200 as tsb
+    from torch_spyre_b200.workloads import DECODE_CONFIGS, context_lens_for
+
+    cfg = DECODE_CONFIGS[args.workload]
+    device = torch.device("cuda", local if world > 1 else 0)
+    steps = args.steps or DEFAULT_STEPS[args.workload]
+    warmup = max(3, args.warmup if args.warmup is not None else 20)
+    tp = cfg.name == "tp70b"
+    if tp and cfg.num_kv_heads % world:
+        raise SystemExit(f"tp70b needs N dividing {cfg.num_kv_heads}")
+
+    # how many rotating input sets keep each step's reads out of L2
+    probe = build_inputs(cfg, rank, world, 1, device)[0]
+    n_sets = max(1, math.ceil(3 * L2_BYTES / probe.kv_bytes)) if probe.kv_bytes < 3 * L2_BYTES else 1
+    n_sets = min(n_sets, 32)
+    sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1)
+    step_bytes = statistics.mean(s.step_bytes for s in sets)
+    kv_bytes = statistics.mean(s.kv_bytes for s in sets)
+    B = len(sets[0].ctx)
+
+    w_o = None
+    if tp:
+        hidden = cfg.hidden
+        hq_local = sets[0].q.shape[1]
+        g = torch.Generator(device=device)
+        g.manual_seed(1234 + rank)
+        # W_o [hidden_out, hidden_in] restricted to this rank's input columns
+        w_o = (torch.randn((hidden, hq_local * cfg.head_dim), generator=g, device=device,
+                           dtype=torch.float16) * 0.02)
+        w_o_t = w_o.t()
+        partial = torch.empty((B, hidden), dtype=torch.float16, device=device)
+
+    def step(s, out=None):
+        o = tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
+        if tp:
+            torch.matmul(o.view(B, -1), w_o_t, out=partial)
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.all_reduce(partial)
+        return o
+
+    stream = torch.cuda.Stream(device)
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in sets:  # warm the op once per set before capture
+            step(s)
+        stream.synchronize()
+        if not (tp and world > 1):
+            for s in sets:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    step(s)
+                graphs.append(g)
+    replay = (lambda i: graphs[i % n_sets].replay()) if graphs else (lambda i: step(sets[i % n_sets]))
+
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            replay(i)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local if world > 1 else 0) as clk:
+            time.sleep(0.25)  # let the sampler start
+            t_all0.record(stream)
+            for i in range(steps):
+                ev[i][0].record(stream)
+                replay(i)
+                ev[i][1].record(stream)
+            t_all1.record(stream)
+            stream.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+    total_ms = max_over_ranks(t_all0.elapsed_time(t_all1), world)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ms_per_step = total_ms / steps
+    tokens_per_step = B if tp else B * world
+    value = tokens_per_step * steps / (total_ms / 1e3)
+
+    peak, peak_kind = hbm_peak()
+    # the decode kernel is the only launch of a replicated step; for tp70b the
+    # per-launch duration covers decode + o_proj (+ all-reduce), so the decode
+    # roofline is reported over the whole step there
+    achieved = step_bytes / (launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                "traffic": profiled_traffic("decode_kernel", args.workload),
+                "kernel": "decode_kernel", "algorithmic_bytes_per_launch": int(step_bytes),
+                "mean_launch_ms": round(launch_ms, 5)}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o_t if tp else None)
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_baseline_seconds > 0:
+        rate, n, el = cpu_oracle_rate(sets[0], args.cpu_baseline_seconds)
+        cpu = {"value": round(rate, 3), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{n} whole sequences of the {args.workload} batch (round robin), {el:.1f} s, "
+                         "paged gather + torch CPU SDPA fp32"}
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+        "data": "synthetic (seeded N(0,1) fp16 q/K/V, seeded contexts and block permutations)",
+        "config": {"workload": args.workload, "description": cfg.description, "batch_per_rank": B,
+                   "global_batch": tokens_per_step, "num_q_heads": cfg.num_q_heads,
+                   "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
+                   "kv_heads_per_rank": sets[0].k_pool.shape[1],
+                   "parallelism": (f"tp{world} (kv-head shards + NCCL all-reduce)" if tp else f"dp{world} (sequence shards)"),
+                   "l2": f"{n_sets} rotating input sets, {kv_bytes / 1e6:.1f} MB KV read per step (L2 126 MB)",
+                   "graphs": bool(graphs)},
+        "kv_gbs": round(kv_bytes / (ms_per_step / 1e3) / 1e9, 1),
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o_t):
+    """Public-API decode step with host buffers: H2D inputs, append, decode, D2H."""
+    s = sets[0]
+    B, hq, D = s.q.shape
+    hkv = s.k_pool.shape[1]
+    ctx = torch.tensor(s.ctx, dtype=torch.int64)
+    pos = (ctx - 1).clamp(min=0)
+    bt_cpu = s.block_table.cpu()
+    slots = (bt_cpu.gather(1, (pos // 64).unsqueeze(1)).squeeze(1).long() * 64 + pos % 64)
+    h = {
+        "q": s.q.cpu().pin_memory(),
+        "k_new": torch.randn((B, hkv, D), dtype=torch.float16).pin_memory(),
+        "v_new": torch.randn((B, hkv, D), dtype=torch.float16).pin_memory(),
+        "slots": slots.pin_memory(),
+        "block_table": bt_cpu.pin_memory(),
+        "context_lens": s.context_lens.cpu().pin_memory(),
+    }
+    d = {k: torch.empty_like(v, device=s.q.device) for k, v in h.items()}
+    out_shape = (B, cfg.hidden) if tp else (B, hq, D)
+    h_out = torch.empty(out_shape, dtype=torch.float16).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in h.values())
+    d2h = h_out.numel() * h_out.element_size()
+    n = max(3, min(steps, 500))
+
+    def one():
+        for k in h:
+            d[k].copy_(h[k], non_blocking=True)
+        tsb.kv_append(d["k_new"], d["v_new"], s.k_pool, s.v_pool, d["slots"])
+        o = tsb.decode_attention(d["q"], s.k_pool, s.v_pool, d["block_table"], d["context_lens"])
+        if tp:
+            r = torch.matmul(o.view(B, -1), w_o_t)
+            if world > 1:
+                import torch.distributed as dist
+
+                dist.all_reduce(r)
+            o = r
+        h_out.copy_(o, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, warmup // 4)):
+            one()
+        stream.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            one()
+        b.record(stream)
+        stream.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b), world) / n
+    tokens = B if tp else B * world
+    return {"value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms, 5),
+            "path": "torch.ops.b200kv.kv_append + decode_attention, pinned host buffers"}
+
+
+# ------------------------------------------------------------- reference ----
+def run_reference(args, rank, world):
+    """The reference's CPU eager decode path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    from torch_spyre_b200.workloads import DECODE_CONFIGS, make_decode_inputs
+
+    cfg = DECODE_CONFIGS[args.workload]
+    steps = args.steps or DEFAULT_STEPS[args.workload]
+    warmup = max(3, args.warmup if args.warmup is not None else 20)
+    kw = {"num_kv_heads": cfg.num_kv_heads // world} if cfg.name == "tp70b" else {}
+    inp = make_decode_inputs(cfg, device="cpu", seed_tag="set0/rank0", **kw)
+    from oracle import paged_attention as opa
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    B = len(inp.ctx)
+    # size each step so the whole run stays within ~2 minutes
+    budget = min(1.0, max(0.002, 120.0 / (steps + warmup)))
+    t0 = time.perf_counter()
+    opa.decode_attention_cpu(inp.q[:1], inp.k_pool, inp.v_pool, inp.block_table[:1], inp.context_lens[:1])
+    t_seq = time.perf_counter() - t0
+    per_step = max(1, min(B, int(budget / max(t_seq, 1e-9))))
+    times, b = [], 0
+    for i in range(warmup + steps):
+        idx = [(b + j) % B for j in range(per_step)]
+        b = (b + per_step) % B
+        t0 = time.perf_counter()
+        opa.decode_attention_cpu(inp.q[idx], inp.k_pool, inp.v_pool, inp.block_table[idx], inp.context_lens[idx])
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = per_step * steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": round(1e3 * total / steps, 4), "higher_is_better": True,
+        "scaling": "strong" if cfg.name == "tp70b" else "weak", "vs_baseline": None, "dtype": "f32 (CPU SDPA)",
+        "data": "synthetic (seeded N(0,1) fp16 q/K/V)",
+        "config": {"workload": args.workload, "description": cfg.description},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": f"{per_step} sequence(s) per step of the {args.workload} batch, "
+                                                   "paged gather + torch CPU SDPA (reference CPU eager path)"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,178 @@
+/*
+ * b200kv.h -- C ABI of the B200 paged-KV decode library (libb200kv.so).
+ *
+ * The library implements one hot path of torch-spyre for NVIDIA B200 (sm_100a):
+ * single-token decode attention over a paged fp16 KV cache that is tiled in
+ * 64-element "sticks", plus the on-device KV append and relayout that feed it.
+ *
+ * Conventions (every entry point):
+ *   - plain C types only; device buffers are raw device pointers, sizes are
+ *     int64_t, the CUDA stream is passed as an opaque `void *` (a cudaStream_t,
+ *     NULL = legacy default stream);
+ *   - return an int status (enum b200kv_status); 0 means success.  A non-zero
+ *     status leaves a message that b200kv_last_error() returns (thread-local);
+ *   - argument validation happens on the host before any launch; nothing is
+ *     allocated and the stream is never synchronised by a compute entry point;
+ *   - device-side index errors (a block id or slot outside the pool) never
+ *     fault: the access is skipped (TMA out-of-bounds fill, or an explicit
+ *     bounds test) and, when `error_flag` is non-NULL, a bit is OR-ed into that
+ *     device int32 (B200KV_DEVERR_*).  The caller reads it when it chooses.
+ *
+ * KV pool layout ("paged stick layout").  One page holds P = 64 consecutive
+ * tokens of one KV head.  Inside a page the head dimension D (= 64 * S) is split
+ * into S sticks of 64 fp16 (128 bytes); the page is the reference's default
+ * stick tiling of a [64, D] fp16 tile: device_size [S, 64, 64], stride_map
+ * [64, D, 1] (torch_spyre/csrc/spyre_tensor_impl.cpp:46-175).  The pool is
+ *     k_pool, v_pool : fp16 [num_blocks, num_kv_heads, S, 64, 64]
+ * so token t of sequence b, element d of head h lives at element offset
+ *     ((blk * Hkv + h) * S + d / 64) * 4096 + (t % 64) * 64 + d % 64,
+ *     blk = block_table[b * block_table_stride + t / 64].
+ * A slot is blk * 64 + (t % 64) (the kv_append addressing).
+ */
+#ifndef B200KV_H_
+#define B200KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define B200KV_API __attribute__((visibility("default")))
+#else
+#define B200KV_API
+#endif
+
+#define B200KV_PAGE_TOKENS 64
+#define B200KV_STICK_ELEMS 64
+
+enum b200kv_status {
+  B200KV_OK = 0,
+  B200KV_ERR_INVALID_ARG = 1,   /* null pointer, bad size, bad stride        */
+  B200KV_ERR_UNSUPPORTED = 2,   /* legal but not implemented (e.g. D != 128) */
+  B200KV_ERR_WORKSPACE = 3,     /* workspace missing or too small            */
+  B200KV_ERR_CUDA = 4,          /* a CUDA runtime / driver call failed       */
+};
+
+/* Bits OR-ed into the optional device-side error flag. */
+#define B200KV_DEVERR_BAD_BLOCK 0x1 /* block id outside [0, num_blocks)       */
+#define B200KV_DEVERR_BAD_SLOT 0x2  /* slot outside [0, num_blocks * 64)      */
+#define B200KV_DEVERR_BAD_LEN 0x4   /* context_len < 0 or > capacity of table */
+#define B200KV_DEVERR_TIMEOUT 0x8   /* a bounded wait on a page transfer expired */
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+B200KV_API int b200kv_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to
+ * len) into buf.  Returns the full message length.  Replaces the reference's
+ * TORCH_CHECK / RuntimeError reporting (torch_spyre/csrc/spyre_mem.cpp:266-293). */
+B200KV_API int b200kv_last_error(char *buf, size_t len);
+
+/* ------------------------------------------------------------------------ *
+ * Stick layout algebra (host only, no GPU needed).
+ * Restates SpyreTensorLayout::init (torch_spyre/csrc/spyre_tensor_impl.cpp:
+ * 126-175; tiling rule get_generic_stick_layout 46-82, stride map 104-124).
+ *   host_size[rank], host_stride[rank] (NULL = contiguous),
+ *   dim_order[order_len] (NULL = identity; order_len == rank, or rank + 1 with
+ *   a trailing -1 for the sparse layout), elem_bytes (2 for fp16, 4 for fp32).
+ * Writes device_rank (= rank + 1, or 2 for a scalar) entries into
+ * device_size / stride_map (capacity `cap`) and returns device_rank through
+ * *out_rank.
+ * ------------------------------------------------------------------------ */
+B200KV_API int b200kv_stick_layout(const int64_t *host_size, const int64_t *host_stride,
+                        int32_t rank, const int32_t *dim_order,
+                        int32_t order_len, int32_t elem_bytes,
+                        int64_t *device_size, int64_t *stride_map, int32_t cap,
+                        int32_t *out_rank);
+
+/* Bytes a layout occupies on the device: 128 B per stick times the product of
+ * the non-stick device dims (spyre_tensor_impl.cpp:287-293). */
+B200KV_API int64_t b200kv_device_size_in_bytes(const int64_t *device_size,
+                                    int32_t device_rank);
+
+/* ------------------------------------------------------------------------ *
+ * Decode attention.
+ * Replaces the decode case of aten::_scaled_dot_product_fused_attention_
+ * overrideable as decomposed by spyre__sdpa_overrideable
+ * (torch_spyre/_inductor/decompositions.py:523-611; backend selection
+ * torch_spyre/csrc/attn_utils.cpp:22-37): out = softmax(q k^T * scale) v with
+ * GQA head mapping kv_head = q_head / (Hq / Hkv) (decompositions.py:560-563),
+ * over a paged KV cache instead of dense k/v.
+ * ------------------------------------------------------------------------ */
+
+/* Workspace bytes the decode call needs (split-KV partials, per-sequence split
+ * metadata, self-resetting completion counters).  The workspace must be zeroed
+ * once before its first use; every successful call leaves it re-usable (the
+ * counters return to zero).  Calls that share a workspace must be ordered on
+ * one stream. */
+B200KV_API int64_t b200kv_decode_workspace_bytes(int64_t batch, int64_t num_q_heads,
+                                      int64_t num_kv_heads, int64_t head_dim);
+
+/*
+ * q            fp16, element (b, h, d) at q[b * q_stride_b + h * q_stride_h + d]
+ * k_pool/v_pool fp16 [num_blocks, num_kv_heads, D/64, 64, 64] (16-byte aligned)
+ * block_table  int32 [batch, *] row stride block_table_stride (elements)
+ * context_lens int32 [batch], each in [0, max_blocks_per_seq * 64]
+ * out          fp16, element (b, h, d) at out[b * out_stride_b + h * out_stride_h + d]
+ * lse          optional fp32 [batch, num_q_heads] (natural-log logsumexp of the
+ *              scaled scores; -inf for an empty context), may be NULL
+ * scale        softmax scale (the reference default is 1/sqrt(D))
+ * num_splits   0 = automatic split-KV partition; otherwise the target number of
+ *              work items per SM wave (tuning knob, 1..64)
+ * workspace    device buffer of at least b200kv_decode_workspace_bytes()
+ * error_flag   optional device int32 (B200KV_DEVERR_* bits are OR-ed in)
+ * Supported: head_dim 128, Hq % Hkv == 0, Hq / Hkv in {1, 2, 4, 8}, batch <= 1024.
+ * An empty context (len 0) yields a zero output row, matching torch CPU SDPA.
+ */
+B200KV_API int b200kv_decode_attention_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
+    const void *v_pool, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * KV append: write one new token row per entry of slot_mapping into the pools.
+ * Replaces the KV-cache write paths of the reference: spyre::overwrite
+ * (torch_spyre/_inductor/customops.py:262-308) and the aten.index_copy.out
+ * CPU fallback used by HF caches (torch_spyre/ops/fallbacks.py:237-259).
+ *   k_new/v_new fp16, row n head h at k_new[n * new_stride_n + h * new_stride_h]
+ *               (head_dim contiguous, 16-byte aligned rows)
+ *   slot_mapping int64 [num_tokens]; slot = block * 64 + offset; a negative
+ *               slot means "padding token, skip"; slot >= num_blocks * 64 sets
+ *               B200KV_DEVERR_BAD_SLOT and is skipped.
+ * Bit-exact copy.  Duplicate slots in one call: last writer is unspecified.
+ * ------------------------------------------------------------------------ */
+B200KV_API int b200kv_kv_append_f16(const void *k_new, const void *v_new,
+                         int64_t new_stride_n, int64_t new_stride_h,
+                         void *k_pool, void *v_pool,
+                         const int64_t *slot_mapping, int64_t num_tokens,
+                         int64_t num_kv_heads, int64_t head_dim,
+                         int64_t num_blocks, int32_t *error_flag, void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * Bulk relayout between a row-major cache [num_tokens, Hkv, D] fp16 and the
+ * paged stick layout.  Token t goes to page block_ids[t / 64], slot t % 64.
+ * Replaces the host<->device stick relayout the reference does in its DMA
+ * descriptors (generate_dci / get_device_stride_infos,
+ * torch_spyre/csrc/spyre_mem.cpp:176-440) with an HBM->HBM kernel.
+ *   direction 0: rows -> pages (pool slots past num_tokens are untouched)
+ *   direction 1: pages -> rows
+ * block_ids int32 [ceil(num_tokens / 64)]; an id outside [0, num_blocks) sets
+ * B200KV_DEVERR_BAD_BLOCK and that page is skipped.  Bit-exact.
+ * ------------------------------------------------------------------------ */
+B200KV_API int b200kv_relayout_f16(void *rows, void *pool, const int32_t *block_ids,
+                        int64_t num_tokens, int64_t num_kv_heads,
+                        int64_t head_dim, int64_t num_blocks, int32_t direction,
+                        int32_t *error_flag, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200KV_H_ */

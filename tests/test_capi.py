@@ -1,0 +1,90 @@
+"""libb200kv.so loads, exports every symbol of include/b200kv.h, and validates
+arguments on the host (no GPU work is launched by these tests)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from torch_spyre_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "b200kv.h"
+
+
+def header_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"B200KV_API\s+[\w\s\*]+?\b(b200kv_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = header_symbols()
+    for name in ("b200kv_decode_attention_f16", "b200kv_kv_append_f16", "b200kv_relayout_f16",
+                 "b200kv_decode_workspace_bytes", "b200kv_last_error", "b200kv_stick_layout"):
+        assert name in syms
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.lib()
+    for name in header_symbols():
+        assert hasattr(lib, name), name
+    assert set(header_symbols()) <= set(_lib.SIGNATURES), "ctypes signatures missing"
+
+
+def test_version_and_last_error():
+    lib = _lib.lib()
+    assert lib.b200kv_version() >= 100
+    n = lib.b200kv_last_error(None, 0)
+    assert n >= 0
+
+
+def test_workspace_bytes():
+    lib = _lib.lib()
+    w = lib.b200kv_decode_workspace_bytes(16, 32, 8, 128)
+    assert w > 0 and w % 256 == 0
+    assert lib.b200kv_decode_workspace_bytes(16, 32, 8, 64) == -1   # head_dim
+    assert lib.b200kv_decode_workspace_bytes(16, 30, 8, 128) == -1  # Hq % Hkv
+
+
+def _decode(**over):
+    args = dict(q=1 << 20, qsb=4096, qsh=128, k=1 << 21, v=1 << 22, bt=1 << 23, bts=4, ctx=1 << 24,
+                out=1 << 25, osb=4096, osh=128, lse=None, B=2, Hq=32, Hkv=8, D=128, NB=10, MB=4,
+                scale=0.088, splits=0, ws=None, wsb=0, flag=None, stream=None)
+    args.update(over)
+    return _lib.lib().b200kv_decode_attention_f16(*args.values())
+
+
+@pytest.mark.parametrize("over,status,msg", [
+    (dict(D=64), 2, "head_dim"),
+    (dict(Hq=24, Hkv=8), 2, "group size"),
+    (dict(Hq=30), 1, "multiple"),
+    (dict(q=None), 1, "null"),
+    (dict(q=(1 << 20) + 2), 1, "aligned"),
+    (dict(bts=2), 1, "block_table_stride"),
+    (dict(splits=65), 1, "num_splits"),
+    (dict(B=2000), 2, "batch"),
+    (dict(scale=float("nan")), 1, "scale"),
+    (dict(), 3, "workspace"),
+])
+def test_decode_argument_checks(over, status, msg):
+    assert _decode(**over) == status
+    assert msg in _lib.last_error()
+
+
+def test_empty_batch_is_ok_without_gpu():
+    assert _decode(B=0) == 0
+
+
+def test_append_and_relayout_checks():
+    lib = _lib.lib()
+    assert lib.b200kv_kv_append_f16(None, None, 0, 0, None, None, None, 0, 8, 128, 4, None, None) == 0
+    assert lib.b200kv_kv_append_f16(None, None, 1024, 128, None, None, None, 3, 8, 128, 4, None, None) == 1
+    assert lib.b200kv_kv_append_f16(16, 16, 1024, 128, 16, 16, 16, 3, 8, 96, 4, None, None) == 2
+    assert lib.b200kv_relayout_f16(16, 16, 16, 64, 8, 128, 4, 2, None, None) == 1
+    assert "direction" in _lib.last_error()
+    assert lib.b200kv_relayout_f16(16, 16, 16, 0, 8, 128, 4, 0, None, None) == 0
+
+
+def test_error_raises_runtime_error():
+    with pytest.raises(RuntimeError, match="B200KV_ERR_INVALID_ARG"):
+        _lib.call("b200kv_relayout_f16", 16, 16, 16, 64, 8, 128, 4, 5, None, None)

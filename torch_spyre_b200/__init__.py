@@ -1,0 +1,25 @@
+"""B200-native paged decode attention + KV relayout/append (torch-spyre hot path).
+
+Importing the package registers the ``torch.ops.b200kv.*`` custom ops; their
+CUDA library (``lib/libb200kv.so``, built by ``python -m torch_spyre_b200.build``)
+is loaded on first use and is the only implementation.
+"""
+
+from . import _lib, layout, ops, workloads  # noqa: F401
+from ._lib import B200KVError
+from .layout import SpyreTensorLayout, empty_pool, page_layout, pool_shape, stick_layout
+from .ops import decode_attention, kv_append, kv_relayout, kv_unrelayout, sdpa_decode
+
+__all__ = [
+    "B200KVError",
+    "SpyreTensorLayout",
+    "decode_attention",
+    "empty_pool",
+    "kv_append",
+    "kv_relayout",
+    "kv_unrelayout",
+    "page_layout",
+    "pool_shape",
+    "sdpa_decode",
+    "stick_layout",
+]

@@ -1,0 +1,136 @@
+"""Stick layout algebra and the paged KV pool layout.
+
+`SpyreTensorLayout` mirrors the reference class of the same name
+(torch_spyre/csrc/spyre_tensor_impl.h:48-146, bound to Python in
+torch_spyre/csrc/module.cpp): a device layout is a ``device_size`` list whose
+last entry is the stick (128 bytes of elements) and a ``stride_map`` giving, for
+every device dim, the host element stride it walks (-1 for dims of size one).
+The arithmetic runs in libb200kv (``b200kv_stick_layout``, host code, no GPU
+needed), so the kernels and Python share one implementation.
+
+The KV pools use the default tiling of a [64, D] fp16 page:
+device_size [D/64, 64, 64], stride_map [64, D, 1].
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+
+PAGE_TOKENS = 64
+STICK_BYTES = 128
+
+_ELEM_BYTES = {
+    torch.float16: 2,
+    torch.bfloat16: 2,
+    torch.float32: 4,
+    torch.int32: 4,
+    torch.int64: 8,
+    torch.int8: 1,
+    torch.uint8: 1,
+}
+
+
+def elems_per_stick(dtype: torch.dtype) -> int:
+    return STICK_BYTES // _ELEM_BYTES[dtype]
+
+
+def stick_layout(
+    host_size: Sequence[int],
+    dtype: torch.dtype = torch.float16,
+    host_stride: Optional[Sequence[int]] = None,
+    dim_order: Optional[Sequence[int]] = None,
+) -> tuple[list[int], list[int]]:
+    """(device_size, stride_map) of the default stick tiling of a host tensor."""
+    rank = len(host_size)
+    cap = rank + 2
+    hs = (ctypes.c_int64 * max(rank, 1))(*host_size)
+    st = (ctypes.c_int64 * max(rank, 1))(*host_stride) if host_stride is not None else None
+    order = (ctypes.c_int32 * len(dim_order))(*dim_order) if dim_order is not None else None
+    dev = (ctypes.c_int64 * cap)()
+    smap = (ctypes.c_int64 * cap)()
+    out_rank = ctypes.c_int32(0)
+    _lib.call(
+        "b200kv_stick_layout",
+        ctypes.cast(hs, ctypes.c_void_p),
+        ctypes.cast(st, ctypes.c_void_p) if st is not None else None,
+        rank,
+        ctypes.cast(order, ctypes.c_void_p) if order is not None else None,
+        len(dim_order) if dim_order is not None else 0,
+        _ELEM_BYTES[dtype],
+        ctypes.cast(dev, ctypes.c_void_p),
+        ctypes.cast(smap, ctypes.c_void_p),
+        cap,
+        ctypes.cast(ctypes.pointer(out_rank), ctypes.c_void_p),
+    )
+    n = out_rank.value
+    return list(dev[:n]), list(smap[:n])
+
+
+class SpyreTensorLayout:
+    """Device layout of a tensor in 128-byte sticks.
+
+    Constructors follow the reference (tests/tensor/test_tensor_layout.py):
+    ``SpyreTensorLayout(host_size, dtype)``,
+    ``SpyreTensorLayout(host_size, host_stride, dtype, dim_order)`` and the
+    explicit ``SpyreTensorLayout(device_size, stride_map, dtype)``.
+    """
+
+    def __init__(self, *args):
+        if len(args) == 2:
+            size, dtype = args
+            self.device_size, self.stride_map = stick_layout(list(size), dtype)
+        elif len(args) == 4:
+            size, stride, dtype, order = args
+            self.device_size, self.stride_map = stick_layout(list(size), dtype, list(stride), list(order))
+        elif len(args) == 3:
+            self.device_size, self.stride_map, dtype = list(args[0]), list(args[1]), args[2]
+            if len(self.device_size) != len(self.stride_map):
+                raise ValueError("device_size and stride_map must have the same length")
+        else:
+            raise TypeError("SpyreTensorLayout(size, dtype) | (size, stride, dtype, dim_order) | "
+                            "(device_size, stride_map, dtype)")
+        self.device_dtype = dtype
+
+    def device_size_in_bytes(self) -> int:
+        arr = (ctypes.c_int64 * len(self.device_size))(*self.device_size)
+        return int(_lib.lib().b200kv_device_size_in_bytes(ctypes.cast(arr, ctypes.c_void_p), len(arr)))
+
+    def _key(self):
+        return (tuple(self.device_size), tuple(self.stride_map), self.device_dtype)
+
+    def __eq__(self, other):
+        return isinstance(other, SpyreTensorLayout) and self._key() == other._key()
+
+    def __hash__(self):
+        return hash(self._key())
+
+    def __repr__(self):
+        return (f"SpyreTensorLayout(device_size={self.device_size}, stride_map={self.stride_map}, "
+                f"device_dtype={self.device_dtype})")
+
+
+def page_layout(head_dim: int = 128) -> SpyreTensorLayout:
+    """Layout of one page: the default tiling of a [64, head_dim] fp16 tile."""
+    return SpyreTensorLayout([PAGE_TOKENS, head_dim], torch.float16)
+
+
+def pool_shape(num_blocks: int, num_kv_heads: int, head_dim: int = 128) -> tuple[int, ...]:
+    """Shape of a K or V pool: [num_blocks, Hkv, head_dim / 64, 64, 64]."""
+    if head_dim % 64:
+        raise ValueError("head_dim must be a multiple of 64")
+    return (num_blocks, num_kv_heads, head_dim // 64, PAGE_TOKENS, 64)
+
+
+def empty_pool(num_blocks: int, num_kv_heads: int, head_dim: int = 128, device=None) -> torch.Tensor:
+    return torch.empty(pool_shape(num_blocks, num_kv_heads, head_dim), dtype=torch.float16, device=device)
+
+
+def slot_of(block_table: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+    """Slots (block * 64 + offset) of token `positions[b]` of each sequence b."""
+    blk = block_table.gather(1, (positions // PAGE_TOKENS).long().unsqueeze(1)).squeeze(1).long()
+    return blk * PAGE_TOKENS + (positions % PAGE_TOKENS).long()

@@ -1,0 +1,305 @@
+"""torch.library custom ops over libb200kv (namespace ``b200kv``).
+
+Operator surface, mirroring the reference's hot-path ops:
+
+* ``b200kv::decode_attention(q, k_pool, v_pool, block_table, context_lens,
+  scale, num_splits) -> (out, lse)`` -- decode SDPA over the paged pools; the
+  reference reaches this math through
+  ``aten::_scaled_dot_product_fused_attention_overrideable``
+  (torch_spyre/csrc/attn_utils.cpp:22-37 -> torch_spyre/_inductor/
+  decompositions.py:523-611).  :func:`sdpa_decode` is the drop-in adapter with
+  the SDPA signature and the reference's output memory order (596-600).
+* ``b200kv::kv_append(k_new, v_new, k_pool!, v_pool!, slot_mapping)`` -- the
+  KV slot write, in place like ``spyre::overwrite`` (customops.py:262-295,
+  ``mutates_args``) and ``Tensor.index_copy_`` (ops/fallbacks.py:256).
+* ``b200kv::kv_relayout(rows, pool!, block_ids)`` /
+  ``b200kv::kv_unrelayout(pool, block_ids, num_tokens) -> rows`` -- the
+  row-major <-> stick-page relayout (spyre_mem.cpp:176-440 as an HBM kernel).
+
+Each op has a ``register_fake`` so it can be traced.  The CUDA library is the
+only implementation: CPU tensors are rejected, there is no fallback.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .layout import PAGE_TOKENS
+
+HEAD_DIM = 128
+
+# ---------------------------------------------------------------- helpers ---
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"b200kv ops run on CUDA devices only (got a tensor on {t.device}); "
+                "there is no CPU fallback"
+            )
+
+
+def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised decode workspace cached per (device, stream).
+
+    The decode kernel leaves its completion counters at zero after every call,
+    so one buffer serves every call ordered on the same stream.
+    """
+    key = (device.index if device.index is not None else torch.cuda.current_device(), _stream_ptr(device))
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _debug_checks() -> bool:
+    return os.environ.get("B200KV_CHECK", "0") not in ("", "0")
+
+
+def _maybe_check_flag(flag: Optional[torch.Tensor], what: str) -> None:
+    if flag is not None and _debug_checks():
+        v = int(flag.item())
+        if v:
+            raise RuntimeError(f"{what}: device error flag 0x{v:x}")
+
+
+def _check_pool(pool: torch.Tensor, name: str) -> None:
+    if pool.dtype != torch.float16 or pool.dim() != 5 or pool.shape[3] != PAGE_TOKENS or pool.shape[4] != 64:
+        raise ValueError(f"{name} must be fp16 [num_blocks, Hkv, D/64, 64, 64], got {tuple(pool.shape)} {pool.dtype}")
+    if not pool.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# --------------------------------------------------------- decode attention --
+@torch.library.custom_op("b200kv::decode_attention", mutates_args=(), device_types="cuda")
+def _decode_attention_op(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_table: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    num_splits: int,
+    error_flag: Optional[torch.Tensor],
+) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda(q, k_pool, v_pool, block_table, context_lens)
+    if q.dim() != 3 or q.dtype != torch.float16:
+        raise ValueError(f"q must be fp16 [B, Hq, D], got {tuple(q.shape)} {q.dtype}")
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    if k_pool.shape != v_pool.shape:
+        raise ValueError("k_pool and v_pool must have the same shape")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.stride(1) != 1:
+        raise ValueError("block_table must be int32 [B, max_blocks] with unit column stride")
+    if context_lens.dtype != torch.int32 or context_lens.dim() != 1 or not context_lens.is_contiguous():
+        raise ValueError("context_lens must be a contiguous int32 [B] tensor")
+    if q.stride(2) != 1:
+        raise ValueError("q must have a contiguous head_dim")
+    B, Hq, D = q.shape
+    NB, Hkv = k_pool.shape[0], k_pool.shape[1]
+    if D != k_pool.shape[2] * 64:
+        raise ValueError(f"q head_dim {D} does not match the pools ({k_pool.shape[2] * 64})")
+    if block_table.shape[0] != B or context_lens.shape[0] != B:
+        raise ValueError("block_table / context_lens batch mismatch")
+    out = torch.empty((B, Hq, D), dtype=torch.float16, device=q.device)
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    if B == 0:
+        return out, lse
+    lib = _lib.lib()
+    wbytes = lib.b200kv_decode_workspace_bytes(B, Hq, Hkv, D)
+    # An unsupported shape has no workspace size; the call below then reports
+    # the precise reason from the library's own argument checks.
+    ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
+    _lib.call(
+        "b200kv_decode_attention_f16",
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_pool.data_ptr(), v_pool.data_ptr(),
+        block_table.data_ptr(), block_table.stride(0),
+        context_lens.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr(),
+        B, Hq, Hkv, D, NB, block_table.shape[1],
+        float(scale), int(num_splits),
+        ws.data_ptr(), ws.numel(),
+        _ptr(error_flag), _stream_ptr(q.device),
+    )
+    _maybe_check_flag(error_flag, "decode_attention")
+    return out, lse
+
+
+@_decode_attention_op.register_fake
+def _(q, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag):
+    B, Hq, D = q.shape
+    return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)
+
+
+def decode_attention(
+    q: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_table: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: Optional[float] = None,
+    num_splits: int = 0,
+    return_lse: bool = False,
+    error_flag: Optional[torch.Tensor] = None,
+):
+    """Decode attention of one new token per sequence over the paged KV pools.
+
+    q [B, Hq, D] fp16; pools fp16 [NB, Hkv, D/64, 64, 64]; block_table int32
+    [B, max_blocks]; context_lens int32 [B].  Returns out [B, Hq, D] fp16 (and
+    the natural-log LSE [B, Hq] fp32 when ``return_lse``).
+    """
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    out, lse = torch.ops.b200kv.decode_attention(
+        q, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
+    )
+    return (out, lse) if return_lse else out
+
+
+# ------------------------------------------------------------------ append --
+@torch.library.custom_op("b200kv::kv_append", mutates_args=("k_pool", "v_pool"), device_types="cuda")
+def _kv_append_op(
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    error_flag: Optional[torch.Tensor],
+) -> None:
+    _require_cuda(k_new, v_new, k_pool, v_pool, slot_mapping)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    if k_new.shape != v_new.shape or k_new.dim() != 3 or k_new.dtype != torch.float16 or v_new.dtype != torch.float16:
+        raise ValueError("k_new / v_new must be fp16 [N, Hkv, D] of equal shape")
+    if k_new.stride() != v_new.stride() or k_new.stride(2) != 1:
+        raise ValueError("k_new / v_new must share strides with a contiguous head_dim")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous int64 [N] tensor")
+    N, Hkv, D = k_new.shape
+    if slot_mapping.shape[0] != N or Hkv != k_pool.shape[1] or D != k_pool.shape[2] * 64:
+        raise ValueError("k_new does not match slot_mapping / the pools")
+    _lib.call(
+        "b200kv_kv_append_f16",
+        k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+        k_pool.data_ptr(), v_pool.data_ptr(), slot_mapping.data_ptr(),
+        N, Hkv, D, k_pool.shape[0], _ptr(error_flag), _stream_ptr(k_new.device),
+    )
+    _maybe_check_flag(error_flag, "kv_append")
+
+
+@_kv_append_op.register_fake
+def _(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag):
+    return None
+
+
+def kv_append(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag=None) -> None:
+    """Writes row n of k_new / v_new ([N, Hkv, D]) into slot slot_mapping[n]."""
+    torch.ops.b200kv.kv_append(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag)
+
+
+# ---------------------------------------------------------------- relayout --
+@torch.library.custom_op("b200kv::kv_relayout", mutates_args=("pool",), device_types="cuda")
+def _kv_relayout_op(rows: torch.Tensor, pool: torch.Tensor, block_ids: torch.Tensor,
+                    error_flag: Optional[torch.Tensor]) -> None:
+    _require_cuda(rows, pool, block_ids)
+    _check_pool(pool, "pool")
+    if rows.dim() != 3 or rows.dtype != torch.float16 or not rows.is_contiguous():
+        raise ValueError("rows must be a contiguous fp16 [T, Hkv, D] tensor")
+    T, Hkv, D = rows.shape
+    if Hkv != pool.shape[1] or D != pool.shape[2] * 64:
+        raise ValueError("rows do not match the pool's heads / head_dim")
+    if block_ids.dtype != torch.int32 or block_ids.dim() != 1 or block_ids.numel() < -(-T // PAGE_TOKENS):
+        raise ValueError("block_ids must be int32 [ceil(T / 64)]")
+    _lib.call("b200kv_relayout_f16", rows.data_ptr(), pool.data_ptr(), block_ids.data_ptr(),
+              T, Hkv, D, pool.shape[0], 0, _ptr(error_flag), _stream_ptr(rows.device))
+    _maybe_check_flag(error_flag, "kv_relayout")
+
+
+@_kv_relayout_op.register_fake
+def _(rows, pool, block_ids, error_flag):
+    return None
+
+
+@torch.library.custom_op("b200kv::kv_unrelayout", mutates_args=(), device_types="cuda")
+def _kv_unrelayout_op(pool: torch.Tensor, block_ids: torch.Tensor, num_tokens: int,
+                      error_flag: Optional[torch.Tensor]) -> torch.Tensor:
+    _require_cuda(pool, block_ids)
+    _check_pool(pool, "pool")
+    Hkv, D = pool.shape[1], pool.shape[2] * 64
+    if block_ids.dtype != torch.int32 or block_ids.dim() != 1 or block_ids.numel() < -(-num_tokens // PAGE_TOKENS):
+        raise ValueError("block_ids must be int32 [ceil(num_tokens / 64)]")
+    rows = torch.empty((num_tokens, Hkv, D), dtype=torch.float16, device=pool.device)
+    _lib.call("b200kv_relayout_f16", rows.data_ptr(), pool.data_ptr(), block_ids.data_ptr(),
+              num_tokens, Hkv, D, pool.shape[0], 1, _ptr(error_flag), _stream_ptr(pool.device))
+    _maybe_check_flag(error_flag, "kv_unrelayout")
+    return rows
+
+
+@_kv_unrelayout_op.register_fake
+def _(pool, block_ids, num_tokens, error_flag):
+    return pool.new_empty((num_tokens, pool.shape[1], pool.shape[2] * 64))
+
+
+def kv_relayout(rows, pool, block_ids, error_flag=None) -> None:
+    """Scatters a row-major cache [T, Hkv, D] into pages block_ids[t // 64]."""
+    torch.ops.b200kv.kv_relayout(rows, pool, block_ids, error_flag)
+
+
+def kv_unrelayout(pool, block_ids, num_tokens: int, error_flag=None) -> torch.Tensor:
+    """Gathers pages block_ids[...] back into a row-major [T, Hkv, D] cache."""
+    return torch.ops.b200kv.kv_unrelayout(pool, block_ids, int(num_tokens), error_flag)
+
+
+# ------------------------------------------------------------ SDPA adapter --
+def sdpa_decode(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    scale: Optional[float] = None,
+    enable_gqa: bool = False,
+) -> torch.Tensor:
+    """Decode SDPA with the signature of F.scaled_dot_product_attention.
+
+    query [B, Hq, 1, D]; key/value dense [B, Hkv, S, D] fp16.  The dense K/V are
+    relaid into stick pages on the device (identity block table) and the paged
+    decode kernel runs.  The result has shape [B, Hq, 1, D] and the memory order
+    [B, 1, Hq, D], like the reference decomposition's output
+    (torch_spyre/_inductor/decompositions.py:592-600).
+    """
+    if query.dim() != 4 or query.shape[2] != 1:
+        raise ValueError("sdpa_decode handles one query position: query must be [B, Hq, 1, D]")
+    B, Hq, _, D = query.shape
+    Hkv, S = key.shape[1], key.shape[2]
+    if Hq != Hkv and not enable_gqa:
+        raise ValueError("Hq != Hkv requires enable_gqa=True")
+    nblk = max(1, -(-S // PAGE_TOKENS))
+    k_pool = torch.empty((B * nblk, Hkv, D // 64, PAGE_TOKENS, 64), dtype=torch.float16, device=query.device)
+    v_pool = torch.empty_like(k_pool)
+    block_table = torch.arange(B * nblk, dtype=torch.int32, device=query.device).view(B, nblk)
+    for b in range(B):
+        ids = block_table[b]
+        kv_relayout(key[b].transpose(0, 1).contiguous(), k_pool, ids)
+        kv_relayout(value[b].transpose(0, 1).contiguous(), v_pool, ids)
+    ctx = torch.full((B,), S, dtype=torch.int32, device=query.device)
+    q3 = query[:, :, 0, :]
+    out = decode_attention(q3, k_pool, v_pool, block_table, ctx, scale=scale)
+    # [B, Hq, D] -> [B, 1, Hq, D] memory order, viewed as [B, Hq, 1, D]
+    return out.unsqueeze(1).transpose(1, 2)
