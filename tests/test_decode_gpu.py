@@ -158,3 +158,26 @@ def test_cuda_graph_capture():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
+
+
+def test_simt_kernel_variant_parity():
+    """The CUDA-core variant (B200KV_DECODE_KERNEL=simt, read once per process)."""
+    import os
+    import subprocess
+    import sys
+
+    code = (
+        "import torch, torch_spyre_b200 as tsb\n"
+        "from oracle import paged_attention as opa\n"
+        "from torch_spyre_b200.workloads import DECODE_CONFIGS, make_decode_inputs\n"
+        "for name, ctx in (('gqa_b16', [1, 65, 257, 3000]), ('tp70b', [64, 129, 4096, 7])):\n"
+        "    inp = make_decode_inputs(DECODE_CONFIGS[name], device='cuda', ctx=ctx)\n"
+        "    out = tsb.decode_attention(inp.q, inp.k_pool, inp.v_pool, inp.block_table, inp.context_lens)\n"
+        "    ref = opa.decode_attention_cpu(inp.q, inp.k_pool, inp.v_pool, inp.block_table, inp.context_lens)\n"
+        "    torch.testing.assert_close(out.cpu().float(), ref.float(), atol=2e-3, rtol=1e-2)\n"
+        "print('simt ok')\n"
+    )
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, B200KV_DECODE_KERNEL="simt", PYTHONPATH=repo)
+    r = subprocess.run([sys.executable, "-c", code], env=env, cwd=repo, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "simt ok" in r.stdout, r.stderr[-3000:]

@@ -19,7 +19,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libb200kv.so"
 INCLUDE = PKG_DIR.parent / "include"
 
-SOURCES = ["capi.cu", "kv_relayout.cu", "decode_attention.cu"]
+SOURCES = ["capi.cu", "kv_relayout.cu", "decode_attention.cu", "decode_mma.cu", "decode_simt.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -34,7 +34,7 @@ def _needs_rebuild() -> bool:
     if not LIB_PATH.exists():
         return True
     mtime = LIB_PATH.stat().st_mtime
-    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     return any(p.stat().st_mtime > mtime for p in deps)
 
 

@@ -1,0 +1,234 @@
+// Pieces shared by the decode kernels: arguments, workspace layout, the
+// split-KV work plan every CTA derives from context_lens, and the last-CTA
+// log-sum-exp combine of split partials.
+#pragma once
+
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace b200kv {
+
+constexpr int kMaxBatch = 1024;
+constexpr int kMaxWorkItems = 8192;
+constexpr int kDefaultItemsPerCta = 4;
+// The completion counters always occupy the same fixed-size region at the
+// start of the workspace, whatever the call's shape, so a workspace shared by
+// calls of different shapes never sees partials where counters are expected.
+constexpr int64_t kMaxCounters = 131072;  // batch * num_kv_heads limit
+constexpr float kLn2 = 0.69314718055994530942f;
+
+struct DecodeArgs {
+  const __half *q;
+  int64_t q_sb, q_sh;
+  const int32_t *block_table;
+  int64_t bt_stride;
+  const int32_t *ctx_lens;
+  __half *out;
+  int64_t o_sb, o_sh;
+  float *lse;
+  int batch, hkv, hq, max_blocks;
+  int64_t num_blocks;
+  float scale_log2;  // scale * log2(e)
+  int target_items;
+  int *counters;     // [batch * hkv] completion tickets, zero between calls
+  float2 *part_ml;   // [slots][G] (max in log2 units, sum of exp2)
+  float *part_o;     // [slots][G][128] unnormalised partial outputs
+  int32_t *error_flag;
+};
+
+struct WorkspaceLayout {
+  int64_t counters_off, ml_off, o_off, total;
+};
+
+inline WorkspaceLayout workspace_layout(int64_t batch, int64_t hq, int64_t hkv) {
+  const int64_t g = hq / hkv;
+  const int64_t slots = kMaxWorkItems + batch * hkv;
+  auto up = [](int64_t x) { return (x + 255) & ~int64_t(255); };
+  WorkspaceLayout w;
+  w.counters_off = 0;
+  w.ml_off = up(kMaxCounters * 4);
+  w.o_off = up(w.ml_off + slots * g * 8);
+  w.total = up(w.o_off + slots * g * kHeadDim * 4);
+  return w;
+}
+
+// Shared-memory footprint of the plan (per-sequence pages, splits, prefix).
+constexpr int kPlanBytes = (3 * kMaxBatch + 1) * 4 + 64 * 4;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Pages of sequence b (its context length clamped to the block table).
+__device__ __forceinline__ int clamped_ctx(const DecodeArgs &a, int b, bool flag_errors) {
+  int ctx = __ldg(a.ctx_lens + b);
+  const int cap = a.max_blocks * kPageTokens;
+  if (ctx < 0 || ctx > cap) {
+    if (flag_errors && a.error_flag) atomicOr(a.error_flag, B200KV_DEVERR_BAD_LEN);
+    ctx = ctx < 0 ? 0 : cap;
+  }
+  return ctx;
+}
+
+struct Plan {
+  int *nb;       // [batch] pages per sequence
+  int *splits;   // [batch] splits per sequence
+  int *prefix;   // [batch + 1] first item of each sequence (b-major, then kv head)
+  int *scratch;  // [64]
+  int chunk;     // pages per split
+  int total_items;
+};
+
+__device__ __forceinline__ Plan plan_view(uint8_t *base) {
+  Plan p;
+  p.nb = reinterpret_cast<int *>(base);
+  p.splits = p.nb + kMaxBatch;
+  p.prefix = p.splits + kMaxBatch;
+  p.scratch = p.prefix + kMaxBatch + 1;
+  p.chunk = 0;
+  p.total_items = 0;
+  return p;
+}
+
+// Every CTA derives the same split-KV partition from context_lens: the chunk
+// C (pages per split) is the page-head count divided by the target number of
+// work items; sequence b gets max(1, ceil(pages_b / C)) splits per KV head.
+// All NT threads of the CTA must call this (it synchronises).
+template <int NT>
+__device__ __forceinline__ void build_plan(const DecodeArgs &a, Plan &p) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = NT / 32;
+  int local_pages = 0;
+  for (int b = tid; b < a.batch; b += NT) {
+    const int nb = (clamped_ctx(a, b, blockIdx.x == 0) + kPageTokens - 1) / kPageTokens;
+    p.nb[b] = nb;
+    local_pages += nb;
+  }
+  {
+    int v = local_pages;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    if (lane == 0) p.scratch[warp] = v;
+  }
+  __syncthreads();
+  int total_pages = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) total_pages += p.scratch[w];
+  const long long page_heads = static_cast<long long>(total_pages) * a.hkv;
+  const int chunk = max(1, static_cast<int>((page_heads + a.target_items - 1) / a.target_items));
+  constexpr int kPer = (kMaxBatch + NT - 1) / NT;
+  int cnt[kPer];
+  int run = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int b = tid * kPer + i;
+    int items = 0;
+    if (b < a.batch) {
+      const int ns = max(1, (p.nb[b] + chunk - 1) / chunk);
+      p.splits[b] = ns;
+      items = ns * a.hkv;
+    }
+    cnt[i] = run;
+    run += items;
+  }
+  int incl = run;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, m);
+    if (lane >= m) incl += y;
+  }
+  __syncthreads();  // page sums read; scratch reused below
+  if (lane == 31) p.scratch[warp] = incl;
+  __syncthreads();
+  int warp_base = 0;
+  for (int w = 0; w < warp; ++w) warp_base += p.scratch[w];
+  const int thread_base = warp_base + incl - run;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int b = tid * kPer + i;
+    if (b < a.batch) p.prefix[b] = thread_base + cnt[i];
+  }
+  if (tid == NT - 1) p.prefix[a.batch] = thread_base + run;
+  __syncthreads();
+  p.chunk = chunk;
+  p.total_items = p.prefix[a.batch];
+}
+
+struct Item {
+  int b, kvh, split, nsplit, p, p_end, ctx;
+};
+
+// Work item `it` (b-major, then KV head, then split) of the plan.
+__device__ __forceinline__ Item decode_item(const DecodeArgs &a, const Plan &pl, int it) {
+  int lo = 0, hi = a.batch - 1;  // largest b with prefix[b] <= it
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pl.prefix[mid] <= it) lo = mid; else hi = mid - 1;
+  }
+  Item r;
+  r.b = lo;
+  r.nsplit = pl.splits[lo];
+  const int rem = it - pl.prefix[lo];
+  r.kvh = rem / r.nsplit;
+  r.split = rem - r.kvh * r.nsplit;
+  const int nb = pl.nb[lo];
+  r.p = r.split * pl.chunk;
+  r.p_end = min(r.p + pl.chunk, nb);
+  if (r.p > r.p_end) r.p = r.p_end;
+  r.ctx = min(nb * kPageTokens, clamped_ctx(a, lo, false));
+  return r;
+}
+
+// Block id of page p of sequence b, clamped into the pool (bad ids are
+// flagged and replaced by block 0 so no transfer leaves the pool).
+__device__ __forceinline__ int page_block(const DecodeArgs &a, int b, int p) {
+  int blk = __ldg(a.block_table + static_cast<int64_t>(b) * a.bt_stride + p);
+  if (blk < 0 || blk >= a.num_blocks) {
+    if (a.error_flag) atomicOr(a.error_flag, B200KV_DEVERR_BAD_BLOCK);
+    blk = 0;
+  }
+  return blk;
+}
+
+// Final output of (b, head h0 + g, d) from an unnormalised accumulator.
+__device__ __forceinline__ void store_out(const DecodeArgs &a, int b, int h, int d, float acc,
+                                          float l) {
+  a.out[b * a.o_sb + h * a.o_sh + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
+}
+__device__ __forceinline__ void store_lse(const DecodeArgs &a, int b, int h, float m, float l) {
+  if (a.lse)
+    a.lse[static_cast<int64_t>(b) * a.hq + h] = l > 0.f ? (m + log2f(l)) * kLn2 : -CUDART_INF_F;
+}
+
+// Log-sum-exp merge of the nsplit partials of (b, kv head), run by the CTA
+// that finished last.  Threads [0, NT) cover the G x 128 outputs.
+template <int G, int NT>
+__device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item &it, int first,
+                                                 int tid) {
+  const int h0 = it.kvh * G;
+  for (int i = tid; i < G * kHeadDim; i += NT) {
+    const int g = i / kHeadDim, d = i % kHeadDim;
+    float mx = -CUDART_INF_F;
+    for (int s = 0; s < it.nsplit; ++s)
+      mx = fmaxf(mx, __ldcg(a.part_ml + static_cast<int64_t>(first + s) * G + g).x);
+    float lsum = 0.f, acc = 0.f;
+    for (int s = 0; s < it.nsplit; ++s) {
+      const float2 ml = __ldcg(a.part_ml + static_cast<int64_t>(first + s) * G + g);
+      const float w = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - mx);
+      lsum = fmaf(ml.y, w, lsum);
+      acc = fmaf(__ldcg(a.part_o + static_cast<int64_t>(first + s) * G * kHeadDim + i), w, acc);
+    }
+    store_out(a, it.b, h0 + g, d, acc, lsum);
+    if (d == 0) store_lse(a, it.b, h0 + g, mx, lsum);
+  }
+}
+
+}  // namespace b200kv
