@@ -53,8 +53,9 @@ inline WorkspaceLayout workspace_layout(int64_t batch, int64_t hq, int64_t hkv) 
   return w;
 }
 
-// Shared-memory footprint of the plan (per-sequence pages, splits, prefix).
-constexpr int kPlanBytes = (3 * kMaxBatch + 1) * 4 + 64 * 4;
+// Shared-memory footprint of the plan (per-sequence pages, splits, clamped
+// context length, item prefix, scratch).
+constexpr int kPlanBytes = (4 * kMaxBatch + 1) * 4 + 64 * 4;
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -81,6 +82,7 @@ __device__ __forceinline__ int clamped_ctx(const DecodeArgs &a, int b, bool flag
 struct Plan {
   int *nb;       // [batch] pages per sequence
   int *splits;   // [batch] splits per sequence
+  int *ctx;      // [batch] context length clamped to the block table
   int *prefix;   // [batch + 1] first item of each sequence (b-major, then kv head)
   int *scratch;  // [64]
   int chunk;     // pages per split
@@ -91,7 +93,8 @@ __device__ __forceinline__ Plan plan_view(uint8_t *base) {
   Plan p;
   p.nb = reinterpret_cast<int *>(base);
   p.splits = p.nb + kMaxBatch;
-  p.prefix = p.splits + kMaxBatch;
+  p.ctx = p.splits + kMaxBatch;
+  p.prefix = p.ctx + kMaxBatch;
   p.scratch = p.prefix + kMaxBatch + 1;
   p.chunk = 0;
   p.total_items = 0;
@@ -108,7 +111,9 @@ __device__ __forceinline__ void build_plan(const DecodeArgs &a, Plan &p) {
   constexpr int kWarps = NT / 32;
   int local_pages = 0;
   for (int b = tid; b < a.batch; b += NT) {
-    const int nb = (clamped_ctx(a, b, blockIdx.x == 0) + kPageTokens - 1) / kPageTokens;
+    const int ctx = clamped_ctx(a, b, blockIdx.x == 0);
+    const int nb = (ctx + kPageTokens - 1) / kPageTokens;
+    p.ctx[b] = ctx;
     p.nb[b] = nb;
     local_pages += nb;
   }
@@ -183,7 +188,7 @@ __device__ __forceinline__ Item decode_item(const DecodeArgs &a, const Plan &pl,
   r.p = r.split * pl.chunk;
   r.p_end = min(r.p + pl.chunk, nb);
   if (r.p > r.p_end) r.p = r.p_end;
-  r.ctx = min(nb * kPageTokens, clamped_ctx(a, lo, false));
+  r.ctx = pl.ctx[lo];
   return r;
 }
 
@@ -229,6 +234,73 @@ __device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item
     store_out(a, it.b, h0 + g, d, acc, lsum);
     if (d == 0) store_lse(a, it.b, h0 + g, mx, lsum);
   }
+}
+
+// Same merge with the split weights staged in shared memory (`scratch`,
+// capacity `cap` floats, shared by the NT threads, which must all call this):
+// the per-split max/sum are read once, each thread then streams its partial
+// outputs with independent, unrolled loads.  Falls back to combine_partials
+// when the splits do not fit.
+template <int G, int NT, typename SyncFn>
+__device__ __forceinline__ void combine_partials_staged(const DecodeArgs &a, const Item &it,
+                                                        int first, int tid, float *scratch,
+                                                        int cap, SyncFn sync) {
+  const int ns = it.nsplit;
+  if (3 * ns * G + 2 * G > cap) {
+    combine_partials<G, NT>(a, it, first, tid);
+    return;
+  }
+  float *w = scratch;                 // [ns][G] weights exp2(m_s - M) / L
+  float *stat = scratch + ns * G;     // M[G], L[G]
+  float *mls = stat + 2 * G;          // [ns][G] (m, l) pairs
+  const float2 *src = a.part_ml + static_cast<int64_t>(first) * G;
+  for (int i = tid; i < ns * G; i += NT) {
+    const float2 ml = __ldcg(src + i);
+    mls[2 * i] = ml.x;
+    mls[2 * i + 1] = ml.y;
+  }
+  sync();
+  if (tid < G) {
+    float mx = -CUDART_INF_F;
+    for (int s = 0; s < ns; ++s) mx = fmaxf(mx, mls[2 * (s * G + tid)]);
+    float l = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float m = mls[2 * (s * G + tid)];
+      l = fmaf(mls[2 * (s * G + tid) + 1], m == -CUDART_INF_F ? 0.f : exp2f(m - mx), l);
+    }
+    stat[tid] = mx;
+    stat[G + tid] = l;
+  }
+  sync();
+  for (int i = tid; i < ns * G; i += NT) {
+    const int g = i % G;
+    const float m = mls[2 * i], mx = stat[g], l = stat[G + g];
+    w[i] = (m == -CUDART_INF_F || !(l > 0.f)) ? 0.f : exp2f(m - mx) / l;
+  }
+  sync();
+  const int h0 = it.kvh * G;
+  for (int i = tid; i < G * kHeadDim; i += NT) {
+    const int g = i / kHeadDim, d = i % kHeadDim;
+    const float *po = a.part_o + static_cast<int64_t>(first) * G * kHeadDim + i;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= ns; s += 4) {
+      const float v0 = __ldcg(po + (s + 0) * G * kHeadDim);
+      const float v1 = __ldcg(po + (s + 1) * G * kHeadDim);
+      const float v2 = __ldcg(po + (s + 2) * G * kHeadDim);
+      const float v3 = __ldcg(po + (s + 3) * G * kHeadDim);
+      acc0 = fmaf(v0, w[(s + 0) * G + g], acc0);
+      acc1 = fmaf(v1, w[(s + 1) * G + g], acc1);
+      acc2 = fmaf(v2, w[(s + 2) * G + g], acc2);
+      acc3 = fmaf(v3, w[(s + 3) * G + g], acc3);
+    }
+    for (; s < ns; ++s) acc0 = fmaf(__ldcg(po + s * G * kHeadDim), w[s * G + g], acc0);
+    const float l = stat[G + g];
+    a.out[it.b * a.o_sb + (h0 + g) * a.o_sh + d] =
+        __float2half_rn(l > 0.f ? (acc0 + acc1) + (acc2 + acc3) : 0.f);
+    if (d == 0) store_lse(a, it.b, h0 + g, stat[g], l);
+  }
+  sync();
 }
 
 }  // namespace b200kv

@@ -10,10 +10,12 @@
 // idle and the kernel bound by HBM.
 //
 // CTA = 1 producer warp + 4 consumer warps, one CTA per SM (persistent):
-//   producer  lane 0 walks this CTA's work items page by page and issues two
-//             3-D TMA loads per page (K, V; 16 KiB each, 128-byte swizzle,
-//             L2 evict-first) into an NST-stage ring, waiting on each stage's
-//             "empty" mbarrier and arming its "full" mbarrier with the bytes;
+//   producer  walks this CTA's work items page by page: block ids are fetched
+//             32 at a time by the whole warp, the item's q rows are staged with
+//             its first page, and lane 0 issues two 3-D TMA loads per page (K, V;
+//             16 KiB each, 128-byte swizzle, L2 evict-first) into an NST-stage
+//             ring, waiting on each stage's "empty" mbarrier and arming its
+//             "full" mbarrier with the bytes;
 //   consumer  warp w owns tokens [16w, 16w + 16) of every page and keeps its
 //             own online-softmax state, so no CTA barrier is taken per page:
 //               S^T[16 t x 8 h] = K[16 t x 128 d] . Q^T   (8 mma, ldmatrix)
@@ -24,7 +26,8 @@
 // At the end of a work item the 4 warps' (m, l, O) are merged in shared
 // memory; a single split writes the fp16 output, otherwise the unnormalised
 // partial goes to the workspace and the CTA that takes the last ticket of the
-// (b, kv head) merges all partials (decode_common.cuh).
+// (b, kv head) merges all partials (decode_common.cuh); the ticket is read one
+// item later so its atomic round trip overlaps useful work.
 #include "decode_kernels.h"
 
 namespace b200kv {
@@ -33,10 +36,16 @@ namespace {
 constexpr int kConsumerWarps = 4;
 constexpr int kMmaThreads = (kConsumerWarps + 1) * 32;
 
+// Staged q of one work item: G rows of 128 fp16, row stride padded to 272 B so
+// the Q^T fragment loads (8 heads x 4 lanes) hit 32 distinct banks.
+constexpr int kQRowBytes = 272;
+constexpr int kQSlotBytes = 8 * kQRowBytes;
+
 template <int NST>
 struct MmaSmem {
   static constexpr int kStageBytes = 2 * kPageBytes;                     // K page + V page
-  static constexpr int kWO = NST * kStageBytes;                          // float [4][128][8]
+  static constexpr int kQ = NST * kStageBytes;                           // q slot per stage
+  static constexpr int kWO = kQ + NST * kQSlotBytes;                     // float [4][128][8]
   static constexpr int kWML = kWO + kConsumerWarps * kHeadDim * 8 * 4;   // float2 [4][8]
   static constexpr int kPlan = kWML + kConsumerWarps * 8 * 8;
   static constexpr int kBars = (kPlan + kPlanBytes + 7) & ~7;            // full[NST], empty[NST]
@@ -126,20 +135,39 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int total_items = pl.total_items;
 
   // ------------------------------------------------------------ producer --
+  // The whole warp fetches the next 32 block ids of an item in one coalesced
+  // load (so page issue never waits on a block-table read) and stages the
+  // item's q rows into the stage of its first page; lane 0 arms the stage's
+  // full barrier and issues the two page loads.
   if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      const uint64_t policy = l2_policy_evict_first();
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-        const Item it = decode_item(a, pl, item);
-        for (int p = it.p; p < it.p_end; ++p) {
-          mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
-          const int page = page_block(a, it.b, p) * a.hkv + it.kvh;
-          uint8_t *dst = smem + stage * L::kStageBytes;
-          mbar_arrive_expect_tx(&full[stage], 2 * kPageBytes);
-          tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
-          tma_load_3d(dst + kPageBytes, &vmap, &full[stage], 0, 0, page, policy);
+    const uint64_t policy = l2_policy_evict_first();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
+      const Item it = decode_item(a, pl, item);
+      for (int base = it.p; base < it.p_end; base += 32) {
+        const int n = min(32, it.p_end - base);
+        const int my_blk = lane < n ? page_block(a, it.b, base + lane) : 0;
+        for (int j = 0; j < n; ++j) {
+          const int blk = __shfl_sync(0xffffffffu, my_blk, j);
+          if (lane == 0) mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
+          __syncwarp();
+          if (base + j == it.p) {  // first page of the item: stage its q rows
+            uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
+            const __half *qg = a.q + it.b * a.q_sb + (it.kvh * G) * a.q_sh;
+            for (int c = lane; c < G * 16; c += 32) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4 *>(qg + (c >> 4) * a.q_sh + (c & 15) * 8));
+              *reinterpret_cast<uint4 *>(qs + (c >> 4) * kQRowBytes + (c & 15) * 16) = v;
+            }
+            __syncwarp();
+          }
+          if (lane == 0) {
+            const int page = blk * a.hkv + it.kvh;
+            uint8_t *dst = smem + stage * L::kStageBytes;
+            mbar_arrive_expect_tx(&full[stage], 2 * kPageBytes);
+            tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
+            tma_load_3d(dst + kPageBytes, &vmap, &full[stage], 0, 0, page, policy);
+          }
           if (++stage == NST) {
             stage = 0;
             phase ^= 1u;
@@ -162,158 +190,189 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int hc = (lane & 3) * 2;     // heads of this lane's accumulator columns
   const int tr = t0 + (lane >> 2);   // token of this lane's S^T rows (and +8)
   const float sc = a.scale_log2;
+  // Completion ticket of the previous split item, checked one item later so
+  // the atomic's round trip overlaps the next item's pages (thread 0 only).
+  int pend_item = -1, pend_ticket = 0;
+  int *s_flag = pl.scratch + 8;      // [0] combine?  [1] item to combine
 
   int stage = 0;
   uint32_t phase = 0;
-  for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-    const Item it = decode_item(a, pl, item);
-    const int h0 = it.kvh * G;
-    uint32_t qb[8][2];
-    if (qh < G) {
-      const __half *qp = a.q + it.b * a.q_sb + (h0 + qh) * a.q_sh + hc;
+  for (int item = blockIdx.x;; item += gridDim.x) {
+    const bool live = item < total_items;
+    if (live) {
+      const Item it = decode_item(a, pl, item);
+      const int h0 = it.kvh * G;
+      uint32_t qb[8][2];
+      float o[8][4];
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        qb[ks][0] = __ldg(reinterpret_cast<const unsigned int *>(qp + ks * 16));
-        qb[ks][1] = __ldg(reinterpret_cast<const unsigned int *>(qp + ks * 16 + 8));
-      }
-    } else {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) qb[ks][0] = qb[ks][1] = 0u;
-    }
-    float o[8][4];
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-    float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
 
-    for (int p = it.p; p < it.p_end; ++p) {
-      const int valid = min(kPageTokens, it.ctx - p * kPageTokens);
-      mbar_wait_bounded(&full[stage], phase, a.error_flag);
-      const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
-      const uint32_t vbase = kbase + kPageBytes;
-      const bool partial = valid < t0 + 16;
-      if (partial) {  // zero this warp's V rows past the context (0 * NaN = NaN in the MMA)
-        for (int idx = lane; idx < 16 * 16; idx += 32) {
-          const int t = t0 + (idx >> 4), c = idx & 15;
-          if (t >= valid) st_shared_zero16(vbase + swz_off(c >> 3, t, c & 7));
+      for (int p = it.p; p < it.p_end; ++p) {
+        const int valid = min(kPageTokens, it.ctx - p * kPageTokens);
+        mbar_wait_bounded(&full[stage], phase, a.error_flag);
+        const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
+        const uint32_t vbase = kbase + kPageBytes;
+        if (p == it.p) {  // q of this item, staged with its first page
+          const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes + hc * 2;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            uint32_t x0 = 0u, x1 = 0u;
+            if (qh < G) {
+              asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x0) : "r"(qs + ks * 32));
+              asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x1) : "r"(qs + ks * 32 + 16));
+            }
+            qb[ks][0] = x0;
+            qb[ks][1] = x1;
+          }
         }
+        const bool partial = valid < t0 + 16;
+        if (partial) {  // zero this warp's V rows past the context (0 * NaN = NaN in the MMA)
+          for (int idx = lane; idx < 16 * 16; idx += 32) {
+            const int t = t0 + (idx >> 4), c = idx & 15;
+            if (t >= valid) st_shared_zero16(vbase + swz_off(c >> 3, t, c & 7));
+          }
+          __syncwarp();
+        }
+        // S^T = K . Q^T over the 128 dims (two independent accumulation chains)
+        float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ks += 2) {
+          uint32_t ka[4], kb[4];
+          const int d = ks * 16 + k_dof;
+          ldsm_x4(kbase + swz_off(d >> 6, k_row, (d & 63) >> 3), ka);
+          ldsm_x4(kbase + swz_off((d + 16) >> 6, k_row, ((d + 16) & 63) >> 3), kb);
+          mma16816(s, ka, qb[ks][0], qb[ks][1]);
+          mma16816(s2, kb, qb[ks + 1][0], qb[ks + 1][1]);
+        }
+        // online softmax over this warp's 16 tokens, heads hc and hc + 1
+        const float x0 = tr < valid ? (s[0] + s2[0]) * sc : -CUDART_INF_F;
+        const float x1 = tr < valid ? (s[1] + s2[1]) * sc : -CUDART_INF_F;
+        const float x2 = tr + 8 < valid ? (s[2] + s2[2]) * sc : -CUDART_INF_F;
+        const float x3 = tr + 8 < valid ? (s[3] + s2[3]) * sc : -CUDART_INF_F;
+        const float mn0 = fmaxf(m0, quad_max(fmaxf(x0, x2)));
+        const float mn1 = fmaxf(m1, quad_max(fmaxf(x1, x3)));
+        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f, al0 = 1.f, al1 = 1.f;
+        if (mn0 != -CUDART_INF_F) {
+          p0 = exp2f(x0 - mn0);
+          p2 = exp2f(x2 - mn0);
+          al0 = exp2f(m0 - mn0);
+        }
+        if (mn1 != -CUDART_INF_F) {
+          p1 = exp2f(x1 - mn1);
+          p3 = exp2f(x3 - mn1);
+          al1 = exp2f(m1 - mn1);
+        }
+        l0 = l0 * al0 + quad_sum(p0 + p2);
+        l1 = l1 * al1 + quad_sum(p1 + p3);
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][0] *= al0;
+          o[mt][1] *= al1;
+          o[mt][2] *= al0;
+          o[mt][3] *= al1;
+        }
+        const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the warp
+        const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
+        // O^T += V^T . P^T, 8 tiles of 16 dims
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d = mt * 16 + v_dof;
+          uint32_t va[4];
+          ldsm_x4_t(vbase + swz_off(d >> 6, v_row, (d & 63) >> 3), va);
+          mma16816(o[mt], va, pb0, pb1);
+        }
+        if (partial) fence_proxy_async_smem();  // zero stores before the next TMA write
         __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == NST) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
-      // S^T = K . Q^T over the 128 dims
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int d = ks * 16 + k_dof;
-        uint32_t ka[4];
-        ldsm_x4(kbase + swz_off(d >> 6, k_row, (d & 63) >> 3), ka);
-        mma16816(s, ka, qb[ks][0], qb[ks][1]);
-      }
-      // online softmax over this warp's 16 tokens, heads hc and hc + 1
-      const float x0 = tr < valid ? s[0] * sc : -CUDART_INF_F;
-      const float x1 = tr < valid ? s[1] * sc : -CUDART_INF_F;
-      const float x2 = tr + 8 < valid ? s[2] * sc : -CUDART_INF_F;
-      const float x3 = tr + 8 < valid ? s[3] * sc : -CUDART_INF_F;
-      const float mn0 = fmaxf(m0, quad_max(fmaxf(x0, x2)));
-      const float mn1 = fmaxf(m1, quad_max(fmaxf(x1, x3)));
-      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f, al0 = 1.f, al1 = 1.f;
-      if (mn0 != -CUDART_INF_F) {
-        p0 = exp2f(x0 - mn0);
-        p2 = exp2f(x2 - mn0);
-        al0 = exp2f(m0 - mn0);
-      }
-      if (mn1 != -CUDART_INF_F) {
-        p1 = exp2f(x1 - mn1);
-        p3 = exp2f(x3 - mn1);
-        al1 = exp2f(m1 - mn1);
-      }
-      l0 = l0 * al0 + quad_sum(p0 + p2);
-      l1 = l1 * al1 + quad_sum(p1 + p3);
-      m0 = mn0;
-      m1 = mn1;
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        o[mt][0] *= al0;
-        o[mt][1] *= al1;
-        o[mt][2] *= al0;
-        o[mt][3] *= al1;
-      }
-      const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the warp
-      const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
-      // O^T += V^T . P^T, 8 tiles of 16 dims
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int d = mt * 16 + v_dof;
-        uint32_t va[4];
-        ldsm_x4_t(vbase + swz_off(d >> 6, v_row, (d & 63) >> 3), va);
-        mma16816(o[mt], va, pb0, pb1);
-      }
-      if (partial) fence_proxy_async_smem();  // zero stores before the next TMA write
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      if (++stage == NST) {
-        stage = 0;
-        phase ^= 1u;
-      }
-    }
 
-    // ---- merge the 4 warps' states -------------------------------------
-    if (lane < 4) {
-      s_wml[warp * 8 + hc] = make_float2(m0, l0);
-      s_wml[warp * 8 + hc + 1] = make_float2(m1, l1);
-    }
+      // ---- merge the 4 warps' states -----------------------------------
+      if (lane < 4) {
+        s_wml[warp * 8 + hc] = make_float2(m0, l0);
+        s_wml[warp * 8 + hc + 1] = make_float2(m1, l1);
+      }
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      const int d = mt * 16 + (lane >> 2);
-      float *w = s_wo + (warp * kHeadDim + d) * 8 + hc;
-      *reinterpret_cast<float2 *>(w) = make_float2(o[mt][0], o[mt][1]);
-      *reinterpret_cast<float2 *>(w + 8 * 8) = make_float2(o[mt][2], o[mt][3]);
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d = mt * 16 + (lane >> 2);
+        float *w = s_wo + (warp * kHeadDim + d) * 8 + hc;
+        *reinterpret_cast<float2 *>(w) = make_float2(o[mt][0], o[mt][1]);
+        *reinterpret_cast<float2 *>(w + 8 * 8) = make_float2(o[mt][2], o[mt][3]);
+      }
+      consumer_sync();
+      const int d = tid;  // 128 consumer threads, one output dim each
+      float acc[G], mx[G], ls[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float m = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, s_wml[w * 8 + g].x);
+        float l = 0.f, x = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float2 ml = s_wml[w * 8 + g];
+          const float sc_w = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - m);
+          l = fmaf(ml.y, sc_w, l);
+          x = fmaf(s_wo[(w * kHeadDim + d) * 8 + g], sc_w, x);
+        }
+        acc[g] = x;
+        mx[g] = m;
+        ls[g] = l;
+      }
+      if (it.nsplit == 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          store_out(a, it.b, h0 + g, d, acc[g], ls[g]);
+          if (d == 0) store_lse(a, it.b, h0 + g, mx[g], ls[g]);
+        }
+      } else {
+        float *po = a.part_o + static_cast<int64_t>(item) * G * kHeadDim;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          __stcg(po + g * kHeadDim + d, acc[g]);
+          if (d == 0) __stcg(a.part_ml + static_cast<int64_t>(item) * G + g, make_float2(mx[g], ls[g]));
+        }
+      }
+    }
+    // ---- completion tickets (split items) and deferred combine ------------
+    consumer_sync();  // partial stores of every consumer thread precede the ticket
+    if (tid == 0) {
+      s_flag[0] = 0;
+      if (pend_item >= 0) {
+        const Item pit = decode_item(a, pl, pend_item);
+        if (pend_ticket == pit.nsplit - 1) {
+          s_flag[0] = 1;
+          s_flag[1] = pend_item;
+        }
+        pend_item = -1;
+      }
+      if (live) {
+        const Item it = decode_item(a, pl, item);
+        if (it.nsplit > 1) {
+          __threadfence();  // release this CTA's partial (cumulative over the barrier)
+          pend_ticket = atomicAdd(a.counters + it.b * a.hkv + it.kvh, 1);
+          pend_item = item;
+        }
+      }
+      s_flag[2] = live || pend_item >= 0;  // one drain round settles the last ticket
     }
     consumer_sync();
-    const int d = tid;  // 128 consumer threads, one output dim each
-    float acc[G], mx[G], ls[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float m = -CUDART_INF_F;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, s_wml[w * 8 + g].x);
-      float l = 0.f, x = 0.f;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float2 ml = s_wml[w * 8 + g];
-        const float sc_w = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - m);
-        l = fmaf(ml.y, sc_w, l);
-        x = fmaf(s_wo[(w * kHeadDim + d) * 8 + g], sc_w, x);
-      }
-      acc[g] = x;
-      mx[g] = m;
-      ls[g] = l;
+    if (s_flag[0]) {
+      const Item cit = decode_item(a, pl, s_flag[1]);
+      __threadfence();  // acquire the other CTAs' partials
+      combine_partials_staged<G, kConsumerWarps * 32>(a, cit, s_flag[1] - cit.split, tid, s_wo,
+                                                      kConsumerWarps * kHeadDim * 8, consumer_sync);
+      if (tid == 0) atomicExch(a.counters + cit.b * a.hkv + cit.kvh, 0);
     }
-    if (it.nsplit == 1) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        store_out(a, it.b, h0 + g, d, acc[g], ls[g]);
-        if (d == 0) store_lse(a, it.b, h0 + g, mx[g], ls[g]);
-      }
-    } else {
-      float *po = a.part_o + static_cast<int64_t>(item) * G * kHeadDim;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        __stcg(po + g * kHeadDim + d, acc[g]);
-        if (d == 0) __stcg(a.part_ml + static_cast<int64_t>(item) * G + g, make_float2(mx[g], ls[g]));
-      }
-      __threadfence();
-      consumer_sync();
-      if (tid == 0) {
-        const int ticket = atomicAdd(a.counters + it.b * a.hkv + it.kvh, 1);
-        pl.scratch[8] = ticket == it.nsplit - 1;
-      }
-      consumer_sync();
-      if (pl.scratch[8]) {
-        __threadfence();
-        combine_partials<G, kConsumerWarps * 32>(a, it, item - it.split, tid);
-        if (tid == 0) atomicExch(a.counters + it.b * a.hkv + it.kvh, 0);
-      }
-    }
-    consumer_sync();  // s_wo / s_wml / scratch are reused by the next item
+    const bool more = s_flag[2] != 0;
+    consumer_sync();  // s_wo / s_wml / flags are reused by the next round
+    if (!more) break;
   }
 }
 
@@ -339,7 +398,7 @@ int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int 
   return B200KV_OK;
 }
 
-constexpr int kMmaStages = 6;
+constexpr int kMmaStages = 5;
 
 }  // namespace
 
