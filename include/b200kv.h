@@ -119,8 +119,10 @@ B200KV_API int64_t b200kv_decode_workspace_bytes(int64_t batch, int64_t num_q_he
  * lse          optional fp32 [batch, num_q_heads] (natural-log logsumexp of the
  *              scaled scores; -inf for an empty context), may be NULL
  * scale        softmax scale (the reference default is 1/sqrt(D))
- * num_splits   0 = automatic split-KV partition; otherwise the target number of
- *              work items per SM wave (tuning knob, 1..64)
+ * num_splits   0 = automatic: the KV stream of the whole batch is cut into one
+ *              equal partition per SM; n > 0 = n equal partitions (n <= 8192).
+ *              A sequence-head cut by a partition boundary is a split whose
+ *              partials are merged with a log-sum-exp combine.
  * workspace    device buffer of at least b200kv_decode_workspace_bytes()
  * error_flag   optional device int32 (B200KV_DEVERR_* bits are OR-ed in)
  * Supported: head_dim 128, Hq % Hkv == 0, Hq / Hkv in {1, 2, 4, 8}, batch <= 1024.

@@ -95,7 +95,7 @@ def test_long_context_parity():
 
 
 @pytest.mark.parametrize("group", [1, 2, 4, 8])
-@pytest.mark.parametrize("splits", [1, 4, 64])
+@pytest.mark.parametrize("splits", [1, 4, 64, 1000])
 def test_groups_and_splits(group, splits):
     cfg = DECODE_CONFIGS["gqa_b16"]
     ctx = [1, 63, 64, 65, 257, 1000, 4097, 0]

@@ -74,7 +74,10 @@ extern "C" int b200kv_decode_attention_f16(
   B200KV_CHECK_ARG(num_blocks > 0 && max_blocks_per_seq > 0, "num_blocks and max_blocks_per_seq must be > 0");
   B200KV_CHECK_ARG(max_blocks_per_seq * kPageTokens < (int64_t{1} << 31), "max_blocks_per_seq too large");
   B200KV_CHECK_ARG(block_table_stride >= max_blocks_per_seq, "block_table_stride < max_blocks_per_seq");
-  B200KV_CHECK_ARG(num_splits >= 0 && num_splits <= 64, "num_splits must be in [0, 64]");
+  B200KV_CHECK_ARG(num_splits >= 0 && num_splits <= kMaxWorkItems, "num_splits must be in [0, %d]",
+                   kMaxWorkItems);
+  if (batch * num_kv_heads * max_blocks_per_seq >= (int64_t{1} << 31))
+    return set_error(B200KV_ERR_UNSUPPORTED, "batch * num_kv_heads * max_blocks_per_seq >= 2^31");
   B200KV_CHECK_ARG(std::isfinite(scale), "scale must be finite");
   if (batch == 0) return B200KV_OK;
   B200KV_CHECK_ARG(q && k_pool && v_pool && block_table && context_lens && out,
@@ -117,8 +120,13 @@ extern "C" int b200kv_decode_attention_f16(
   a.part_ml = reinterpret_cast<float2 *>(ws + wl.ml_off);
   a.part_o = reinterpret_cast<float *>(ws + wl.o_off);
   a.error_flag = error_flag;
-  const int per_cta = num_splits > 0 ? static_cast<int>(num_splits) : kDefaultItemsPerCta;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (use_simt_kernel()) return launch_decode_simt(static_cast<int>(group), km, vm, a, per_cta, s);
-  return launch_decode_mma(static_cast<int>(group), km, vm, a, per_cta, s);
+  if (use_simt_kernel()) {
+    // CUDA-core variant: num_splits is its target number of work items per CTA
+    const int per_cta = num_splits > 0 ? static_cast<int>(num_splits < 64 ? num_splits : 64)
+                                       : kDefaultItemsPerCta;
+    return launch_decode_simt(static_cast<int>(group), km, vm, a, per_cta, s);
+  }
+  // tensor-core kernel: num_splits is the number of equal KV partitions (CTAs)
+  return launch_decode_mma(static_cast<int>(group), km, vm, a, static_cast<int>(num_splits), s);
 }

@@ -192,6 +192,100 @@ __device__ __forceinline__ Item decode_item(const DecodeArgs &a, const Plan &pl,
   return r;
 }
 
+// ---------------------------------------------------------------------------
+// Balanced ("stream-K") partition used by the tensor-core kernel.
+//
+// The work is a sequence of units: (b, kv head) pairs in b-major order, pair j
+// contributing w_b = max(pages_b, 1) units (an empty sequence still costs one
+// unit so its zero output has an owner).  CTA c of the grid takes the units
+// [c * per, (c + 1) * per), per = ceil(total / grid), so every CTA streams the
+// same number of pages whatever the spread of context lengths.  A pair cut by
+// CTA boundaries is a split: its piece in CTA c writes a partial to slot
+// j + c (unique, and contiguous from j + c_lo for the pair's pieces), and the
+// CTA that finishes last merges them.
+// ---------------------------------------------------------------------------
+
+// Fills pl.ctx / pl.nb and, in pl.prefix, the exclusive prefix over sequences
+// of w_b; pl.total_items is set to the total number of units (all pairs).
+template <int NT>
+__device__ __forceinline__ void build_unit_plan(const DecodeArgs &a, Plan &p) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kPer = (kMaxBatch + NT - 1) / NT;
+  int cnt[kPer];
+  int run = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int b = tid * kPer + i;
+    int w = 0;
+    if (b < a.batch) {
+      const int ctx = clamped_ctx(a, b, blockIdx.x == 0);
+      const int nb = (ctx + kPageTokens - 1) / kPageTokens;
+      p.ctx[b] = ctx;
+      p.nb[b] = nb;
+      w = max(nb, 1);
+    }
+    cnt[i] = run;
+    run += w;
+  }
+  int incl = run;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, m);
+    if (lane >= m) incl += y;
+  }
+  if (lane == 31) p.scratch[warp] = incl;
+  __syncthreads();
+  int warp_base = 0;
+  for (int w = 0; w < warp; ++w) warp_base += p.scratch[w];
+  const int thread_base = warp_base + incl - run;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int b = tid * kPer + i;
+    if (b < a.batch) p.prefix[b] = thread_base + cnt[i];
+  }
+  if (tid == NT - 1) p.prefix[a.batch] = thread_base + run;
+  __syncthreads();
+  p.total_items = p.prefix[a.batch] * a.hkv;
+  p.chunk = 0;
+}
+
+struct Seg {
+  int b, kvh, pair;     // sequence, KV head, pair index b * Hkv + kvh
+  int p, p_end, ctx;    // pages [p, p_end) of the pair streamed by this piece
+  int nsplit, split;    // pieces of the pair, index of this one
+  int first_slot, slot; // partial slots: pair's first, this piece's
+  int u_next;           // first unit after this piece
+};
+
+// The piece of work that starts at unit u inside CTA c's range [.., u_end).
+__device__ __forceinline__ Seg locate_seg(const DecodeArgs &a, const Plan &pl, int u, int u_end,
+                                          int c, int per) {
+  int lo = 0, hi = a.batch - 1;  // largest b whose first unit is <= u
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a.hkv * pl.prefix[mid] <= u) lo = mid; else hi = mid - 1;
+  }
+  Seg s;
+  s.b = lo;
+  const int nb = pl.nb[lo];
+  const int w = max(nb, 1);
+  const int base = a.hkv * pl.prefix[lo];
+  s.kvh = (u - base) / w;
+  const int pj = base + s.kvh * w;  // first unit of the pair
+  const int hi_u = min(u_end, pj + w);
+  s.pair = lo * a.hkv + s.kvh;
+  s.p = min(u - pj, nb);
+  s.p_end = min(hi_u - pj, nb);
+  s.ctx = pl.ctx[lo];
+  const int c_lo = pj / per, c_hi = (pj + w - 1) / per;
+  s.nsplit = c_hi - c_lo + 1;
+  s.split = c - c_lo;
+  s.first_slot = s.pair + c_lo;
+  s.slot = s.pair + c;
+  s.u_next = hi_u;
+  return s;
+}
+
 // Block id of page p of sequence b, clamped into the pool (bad ids are
 // flagged and replaced by block 0 so no transfer leaves the pool).
 __device__ __forceinline__ int page_block(const DecodeArgs &a, int b, int p) {

@@ -10,9 +10,12 @@
 // idle and the kernel bound by HBM.
 //
 // CTA = 1 producer warp + 4 consumer warps, one CTA per SM (persistent):
-//   producer  walks this CTA's work items page by page: block ids are fetched
-//             32 at a time by the whole warp, the item's q rows are staged with
-//             its first page, and lane 0 issues two 3-D TMA loads per page (K, V;
+// Work partition: the balanced unit split of decode_common.cuh (every CTA
+// streams the same number of pages; a sequence-head cut by a CTA boundary is
+// a split).
+//   producer  walks this CTA's pieces page by page: block ids are fetched
+//             32 at a time by the whole warp, the piece's q rows are staged
+//             with its first page, and lane 0 issues two 3-D TMA loads per page (K, V;
 //             16 KiB each, 128-byte swizzle, L2 evict-first) into an NST-stage
 //             ring, waiting on each stage's "empty" mbarrier and arming its
 //             "full" mbarrier with the bytes;
@@ -23,11 +26,11 @@
 //               P^T fragment from S^T by movmatrix.trans
 //               O^T[128 d x 8 h] += V^T[128 d x 16 t] . P^T (8 mma, ldmatrix.trans)
 //             then one arrive on the stage's empty barrier.
-// At the end of a work item the 4 warps' (m, l, O) are merged in shared
+// At the end of a piece the 4 warps' (m, l, O) are merged in shared
 // memory; a single split writes the fp16 output, otherwise the unnormalised
 // partial goes to the workspace and the CTA that takes the last ticket of the
 // (b, kv head) merges all partials (decode_common.cuh); the ticket is read one
-// item later so its atomic round trip overlaps useful work.
+// piece later so its atomic round trip overlaps useful work.
 #include "decode_kernels.h"
 
 namespace b200kv {
@@ -36,7 +39,7 @@ namespace {
 constexpr int kConsumerWarps = 4;
 constexpr int kMmaThreads = (kConsumerWarps + 1) * 32;
 
-// Staged q of one work item: G rows of 128 fp16, row stride padded to 272 B so
+// Staged q of one piece: G rows of 128 fp16, row stride padded to 272 B so
 // the Q^T fragment loads (8 heads x 4 lanes) hit 32 distinct banks.
 constexpr int kQRowBytes = 272;
 constexpr int kQSlotBytes = 8 * kQRowBytes;
@@ -131,20 +134,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
     fence_mbar_init();
   }
-  build_plan<kMmaThreads>(a, pl);  // synchronises the CTA
-  const int total_items = pl.total_items;
+  build_unit_plan<kMmaThreads>(a, pl);  // synchronises the CTA
+  const int total_units = pl.total_items;
+  const int per = max(1, (total_units + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x));
+  const int c = blockIdx.x;
+  const int u_begin = min(c * per, total_units);
+  const int u_end = min(u_begin + per, total_units);
 
   // ------------------------------------------------------------ producer --
-  // The whole warp fetches the next 32 block ids of an item in one coalesced
+  // The whole warp fetches the next 32 block ids of a piece in one coalesced
   // load (so page issue never waits on a block-table read) and stages the
-  // item's q rows into the stage of its first page; lane 0 arms the stage's
+  // piece's q rows into the stage of its first page; lane 0 arms the stage's
   // full barrier and issues the two page loads.
   if (warp == kConsumerWarps) {
     const uint64_t policy = l2_policy_evict_first();
     int stage = 0;
     uint32_t phase = 0;
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
-      const Item it = decode_item(a, pl, item);
+    for (int u = u_begin; u < u_end;) {
+      const Seg it = locate_seg(a, pl, u, u_end, c, per);
+      u = it.u_next;
       for (int base = it.p; base < it.p_end; base += 32) {
         const int n = min(32, it.p_end - base);
         const int my_blk = lane < n ? page_block(a, it.b, base + lane) : 0;
@@ -152,7 +160,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           const int blk = __shfl_sync(0xffffffffu, my_blk, j);
           if (lane == 0) mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
           __syncwarp();
-          if (base + j == it.p) {  // first page of the item: stage its q rows
+          if (base + j == it.p) {  // first page of the piece: stage its q rows
             uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
             const __half *qg = a.q + it.b * a.q_sb + (it.kvh * G) * a.q_sh;
             for (int c = lane; c < G * 16; c += 32) {
@@ -190,17 +198,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int hc = (lane & 3) * 2;     // heads of this lane's accumulator columns
   const int tr = t0 + (lane >> 2);   // token of this lane's S^T rows (and +8)
   const float sc = a.scale_log2;
-  // Completion ticket of the previous split item, checked one item later so
-  // the atomic's round trip overlaps the next item's pages (thread 0 only).
-  int pend_item = -1, pend_ticket = 0;
-  int *s_flag = pl.scratch + 8;      // [0] combine?  [1] item to combine
+  // Completion ticket of the previous split piece, checked one piece later so
+  // the atomic's round trip overlaps the next piece's pages (thread 0 only).
+  bool pend = false;
+  int pend_ticket = 0, pend_b = 0, pend_kvh = 0, pend_nsplit = 0, pend_first = 0;
+  int *s_flag = pl.scratch + 8;  // [0] combine? [1] b [2] kvh [3] nsplit [4] first slot [5] more
 
   int stage = 0;
   uint32_t phase = 0;
-  for (int item = blockIdx.x;; item += gridDim.x) {
-    const bool live = item < total_items;
+  for (int u = u_begin;;) {
+    const bool live = u < u_end;
+    Seg it;
     if (live) {
-      const Item it = decode_item(a, pl, item);
+      it = locate_seg(a, pl, u, u_end, c, per);
+      u = it.u_next;
       const int h0 = it.kvh * G;
       uint32_t qb[8][2];
       float o[8][4];
@@ -213,7 +224,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         mbar_wait_bounded(&full[stage], phase, a.error_flag);
         const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
         const uint32_t vbase = kbase + kPageBytes;
-        if (p == it.p) {  // q of this item, staged with its first page
+        if (p == it.p) {  // q of this piece, staged with its first page
           const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes + hc * 2;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
@@ -332,52 +343,59 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           if (d == 0) store_lse(a, it.b, h0 + g, mx[g], ls[g]);
         }
       } else {
-        float *po = a.part_o + static_cast<int64_t>(item) * G * kHeadDim;
+        float *po = a.part_o + static_cast<int64_t>(it.slot) * G * kHeadDim;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           __stcg(po + g * kHeadDim + d, acc[g]);
-          if (d == 0) __stcg(a.part_ml + static_cast<int64_t>(item) * G + g, make_float2(mx[g], ls[g]));
+          if (d == 0) __stcg(a.part_ml + static_cast<int64_t>(it.slot) * G + g, make_float2(mx[g], ls[g]));
         }
       }
     }
-    // ---- completion tickets (split items) and deferred combine ------------
+    // ---- completion tickets (split pieces) and deferred combine -----------
     consumer_sync();  // partial stores of every consumer thread precede the ticket
     if (tid == 0) {
       s_flag[0] = 0;
-      if (pend_item >= 0) {
-        const Item pit = decode_item(a, pl, pend_item);
-        if (pend_ticket == pit.nsplit - 1) {
+      if (pend) {
+        if (pend_ticket == pend_nsplit - 1) {
           s_flag[0] = 1;
-          s_flag[1] = pend_item;
+          s_flag[1] = pend_b;
+          s_flag[2] = pend_kvh;
+          s_flag[3] = pend_nsplit;
+          s_flag[4] = pend_first;
         }
-        pend_item = -1;
+        pend = false;
       }
-      if (live) {
-        const Item it = decode_item(a, pl, item);
-        if (it.nsplit > 1) {
-          __threadfence();  // release this CTA's partial (cumulative over the barrier)
-          pend_ticket = atomicAdd(a.counters + it.b * a.hkv + it.kvh, 1);
-          pend_item = item;
-        }
+      if (live && it.nsplit > 1) {
+        __threadfence();  // release this CTA's partial (cumulative over the barrier)
+        pend_ticket = atomicAdd(a.counters + it.pair, 1);
+        pend = true;
+        pend_b = it.b;
+        pend_kvh = it.kvh;
+        pend_nsplit = it.nsplit;
+        pend_first = it.first_slot;
       }
-      s_flag[2] = live || pend_item >= 0;  // one drain round settles the last ticket
+      s_flag[5] = live || pend;  // one drain round settles the last ticket
     }
     consumer_sync();
     if (s_flag[0]) {
-      const Item cit = decode_item(a, pl, s_flag[1]);
+      Item cit;
+      cit.b = s_flag[1];
+      cit.kvh = s_flag[2];
+      cit.nsplit = s_flag[3];
+      cit.split = cit.p = cit.p_end = cit.ctx = 0;
       __threadfence();  // acquire the other CTAs' partials
-      combine_partials_staged<G, kConsumerWarps * 32>(a, cit, s_flag[1] - cit.split, tid, s_wo,
+      combine_partials_staged<G, kConsumerWarps * 32>(a, cit, s_flag[4], tid, s_wo,
                                                       kConsumerWarps * kHeadDim * 8, consumer_sync);
       if (tid == 0) atomicExch(a.counters + cit.b * a.hkv + cit.kvh, 0);
     }
-    const bool more = s_flag[2] != 0;
+    const bool more = s_flag[5] != 0;
     consumer_sync();  // s_wo / s_wml / flags are reused by the next round
     if (!more) break;
   }
 }
 
 template <int G, int NST>
-int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int items_per_cta,
+int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
                cudaStream_t stream) {
   using L = MmaSmem<NST>;
   static_assert(L::kAlloc <= 227 * 1024, "shared memory budget");
@@ -390,9 +408,9 @@ int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int 
     B200KV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
     __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
   }
-  const int grid = sms;  // persistent: one CTA per SM
-  const long long target = static_cast<long long>(grid) * items_per_cta;
-  a.target_items = static_cast<int>(target > kMaxWorkItems ? kMaxWorkItems : target);
+  // one partition (CTA) per SM by default; `partitions` overrides the count
+  const int grid = partitions > 0 ? partitions : sms;
+  a.target_items = grid;
   kern<<<grid, kMmaThreads, L::kAlloc, stream>>>(km, vm, a);
   B200KV_CUDA_TRY(cudaGetLastError());
   return B200KV_OK;
@@ -403,12 +421,12 @@ constexpr int kMmaStages = 5;
 }  // namespace
 
 int launch_decode_mma(int group, const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a,
-                      int items_per_cta, cudaStream_t stream) {
+                      int partitions, cudaStream_t stream) {
   switch (group) {
-    case 1: return launch_mma<1, kMmaStages>(km, vm, a, items_per_cta, stream);
-    case 2: return launch_mma<2, kMmaStages>(km, vm, a, items_per_cta, stream);
-    case 4: return launch_mma<4, kMmaStages>(km, vm, a, items_per_cta, stream);
-    case 8: return launch_mma<8, kMmaStages>(km, vm, a, items_per_cta, stream);
+    case 1: return launch_mma<1, kMmaStages>(km, vm, a, partitions, stream);
+    case 2: return launch_mma<2, kMmaStages>(km, vm, a, partitions, stream);
+    case 4: return launch_mma<4, kMmaStages>(km, vm, a, partitions, stream);
+    case 8: return launch_mma<8, kMmaStages>(km, vm, a, partitions, stream);
     default: return set_error(B200KV_ERR_UNSUPPORTED, "group %d", group);
   }
 }
