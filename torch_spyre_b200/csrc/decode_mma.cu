@@ -416,7 +416,10 @@ int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int 
   return B200KV_OK;
 }
 
-constexpr int kMmaStages = 5;
+#ifndef B200KV_MMA_STAGES
+#define B200KV_MMA_STAGES 5
+#endif
+constexpr int kMmaStages = B200KV_MMA_STAGES;  // 5 stages (160 KiB) fit beside the q slots
 
 }  // namespace
 
