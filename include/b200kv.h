@@ -138,6 +138,25 @@ B200KV_API int b200kv_decode_attention_f16(
     void *workspace, int64_t workspace_bytes, int32_t *error_flag,
     void *stream);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc or any allocator when they
+ * launch decode (an engine replaying pre-planned memory, a plugin host that
+ * only hands over the tensors it owns), so they cannot provide the workspace
+ * of b200kv_decode_attention_f16.  Same arguments minus num_splits and the
+ * workspace; the caller still passes every input and output.  The split-KV
+ * partials go to a 16 MiB scratch array the library keeps on each device that
+ * loads it (until process exit); batch * num_kv_heads must be <= 16384 and the
+ * partials must fit in the scratch (else B200KV_ERR_UNSUPPORTED).  The first
+ * call on a device looks up the scratch address, so make it before any stream
+ * capture.  Calls share the scratch: calls that overlap on the GPU race. */
+B200KV_API int b200kv_decode_attention_f16_noalloc(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
+    const void *v_pool, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int32_t *error_flag, void *stream);
+
 /* ------------------------------------------------------------------------ *
  * KV append: write one new token row per entry of slot_mapping into the pools.
  * Replaces the KV-cache write paths of the reference: spyre::overwrite

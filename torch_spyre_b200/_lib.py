@@ -71,6 +71,13 @@ SIGNATURES = {
             _p, _p,  # error_flag, stream
         ],
     ),
+    "b200kv_decode_attention_f16_noalloc": (
+        ctypes.c_int,
+        [
+            _p, _i64, _i64, _p, _p, _p, _i64, _p, _p, _i64, _i64, _p,
+            _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p,
+        ],
+    ),
     "b200kv_kv_append_f16": (
         ctypes.c_int,
         [_p, _p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p],

@@ -19,7 +19,14 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libb200kv.so"
 INCLUDE = PKG_DIR.parent / "include"
 
-SOURCES = ["capi.cu", "kv_relayout.cu", "decode_attention.cu", "decode_mma.cu", "decode_simt.cu"]
+SOURCES = [
+    "capi.cu",
+    "kv_relayout.cu",
+    "decode_attention.cu",
+    "decode_mma.cu",
+    "decode_simt.cu",
+    "decode_noalloc.cu",
+]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
