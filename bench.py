@@ -230,25 +230,22 @@ def run_ours(args, rank, world, local):
 
     w_o = None
     if tp:
+        from torch_spyre_b200.tp import HeadShard, tp_decode_step
+
+        shard = HeadShard(rank, world, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
         hidden = cfg.hidden
-        hq_local = sets[0].q.shape[1]
         g = torch.Generator(device=device)
         g.manual_seed(1234 + rank)
-        # W_o [hidden_out, hidden_in] restricted to this rank's input columns
-        w_o = (torch.randn((hidden, hq_local * cfg.head_dim), generator=g, device=device,
+        # this rank's input columns of W_o [hidden, Hq * D], N(0, 0.02)
+        w_o = (torch.randn((hidden, len(shard.q_heads) * cfg.head_dim), generator=g, device=device,
                            dtype=torch.float16) * 0.02)
-        w_o_t = w_o.t()
         partial = torch.empty((B, hidden), dtype=torch.float16, device=device)
 
-    def step(s, out=None):
-        o = tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
+    def step(s):
         if tp:
-            torch.matmul(o.view(B, -1), w_o_t, out=partial)
-            if world > 1:
-                import torch.distributed as dist
-
-                dist.all_reduce(partial)
-        return o
+            return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
+                                  out=partial)
+        return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
 
     def decode_only(s):
         return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
@@ -323,7 +320,7 @@ def run_ours(args, rank, world, local):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o_t if tp else None)
+        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o)
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline_seconds > 0:
@@ -355,7 +352,7 @@ def run_ours(args, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
-def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o_t):
+def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
     """Public-API decode step with host buffers: H2D inputs, append, decode, D2H."""
     s = sets[0]
     B, hq, D = s.q.shape
@@ -383,14 +380,14 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o_t):
         for k in h:
             d[k].copy_(h[k], non_blocking=True)
         tsb.kv_append(d["k_new"], d["v_new"], s.k_pool, s.v_pool, d["slots"])
-        o = tsb.decode_attention(d["q"], s.k_pool, s.v_pool, d["block_table"], d["context_lens"])
         if tp:
-            r = torch.matmul(o.view(B, -1), w_o_t)
-            if world > 1:
-                import torch.distributed as dist
+            from torch_spyre_b200.tp import HeadShard, tp_decode_step
 
-                dist.all_reduce(r)
-            o = r
+            shard = HeadShard(int(os.environ.get("RANK", "0")), world, cfg.num_q_heads, cfg.num_kv_heads,
+                              cfg.head_dim)
+            o = tp_decode_step(shard, d["q"], s.k_pool, s.v_pool, d["block_table"], d["context_lens"], w_o)
+        else:
+            o = tsb.decode_attention(d["q"], s.k_pool, s.v_pool, d["block_table"], d["context_lens"])
         h_out.copy_(o, non_blocking=True)
 
     with torch.cuda.stream(stream):
