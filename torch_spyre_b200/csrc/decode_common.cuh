@@ -330,6 +330,43 @@ __device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item
   }
 }
 
+// Merge of at most MAXS partials by 128 threads, thread d producing output dim
+// d of every head: all partial loads are issued before any is used, so the
+// merge costs one memory round trip and no barrier.
+template <int G, int MAXS>
+__device__ __forceinline__ void combine_partials_regs(const DecodeArgs &a, const Item &it,
+                                                      int first, int d) {
+  const int ns = it.nsplit;
+  float2 ml[MAXS][G];
+  float ov[MAXS][G];
+  const float2 *mls = a.part_ml + static_cast<int64_t>(first) * G;
+  const float *po = a.part_o + static_cast<int64_t>(first) * G * kHeadDim + d;
+#pragma unroll
+  for (int s = 0; s < MAXS; ++s)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const bool in = s < ns;
+      ml[s][g] = in ? __ldcg(mls + s * G + g) : make_float2(-CUDART_INF_F, 0.f);
+      ov[s][g] = in ? __ldcg(po + (s * G + g) * kHeadDim) : 0.f;
+    }
+  const int h0 = it.kvh * G;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s) mx = fmaxf(mx, ml[s][g].x);
+    float l = 0.f, acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < MAXS; ++s) {
+      const float w = ml[s][g].x == -CUDART_INF_F ? 0.f : exp2f(ml[s][g].x - mx);
+      l = fmaf(ml[s][g].y, w, l);
+      acc = fmaf(ov[s][g], w, acc);
+    }
+    store_out(a, it.b, h0 + g, d, acc, l);
+    if (d == 0) store_lse(a, it.b, h0 + g, mx, l);
+  }
+}
+
 // Same merge with the split weights staged in shared memory (`scratch`,
 // capacity `cap` floats, shared by the NT threads, which must all call this):
 // the per-split max/sum are read once, each thread then streams its partial

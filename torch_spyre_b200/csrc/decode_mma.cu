@@ -143,9 +143,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 
   // ------------------------------------------------------------ producer --
   // The whole warp fetches the next 32 block ids of a piece in one coalesced
-  // load (so page issue never waits on a block-table read) and stages the
-  // piece's q rows into the stage of its first page; lane 0 arms the stage's
-  // full barrier and issues the two page loads.
+  // load (so page issue never waits on a block-table read); lane 0 arms the
+  // stage's full barrier and issues the two page loads, plus, with the first
+  // page of a piece, one bulk copy per q row into the stage's q slot.
   if (warp == kConsumerWarps) {
     const uint64_t policy = l2_policy_evict_first();
     int stage = 0;
@@ -158,21 +158,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         const int my_blk = lane < n ? page_block(a, it.b, base + lane) : 0;
         for (int j = 0; j < n; ++j) {
           const int blk = __shfl_sync(0xffffffffu, my_blk, j);
-          if (lane == 0) mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
-          __syncwarp();
-          if (base + j == it.p) {  // first page of the piece: stage its q rows
-            uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
-            const __half *qg = a.q + it.b * a.q_sb + (it.kvh * G) * a.q_sh;
-            for (int c = lane; c < G * 16; c += 32) {
-              const uint4 v = __ldg(reinterpret_cast<const uint4 *>(qg + (c >> 4) * a.q_sh + (c & 15) * 8));
-              *reinterpret_cast<uint4 *>(qs + (c >> 4) * kQRowBytes + (c & 15) * 16) = v;
-            }
-            __syncwarp();
-          }
           if (lane == 0) {
+            mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
             const int page = blk * a.hkv + it.kvh;
             uint8_t *dst = smem + stage * L::kStageBytes;
-            mbar_arrive_expect_tx(&full[stage], 2 * kPageBytes);
+            const bool first = base + j == it.p;
+            mbar_arrive_expect_tx(&full[stage], 2 * kPageBytes + (first ? G * kHeadDim * 2 : 0));
+            if (first) {  // the piece's q rows ride on its first page's barrier
+              uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
+              const __half *qg = a.q + it.b * a.q_sb + (it.kvh * G) * a.q_sh;
+#pragma unroll
+              for (int g = 0; g < G; ++g) bulk_load(qs + g * kQRowBytes, qg + g * a.q_sh, kHeadDim * 2, &full[stage]);
+            }
             tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
             tma_load_3d(dst + kPageBytes, &vmap, &full[stage], 0, 0, page, policy);
           }
@@ -366,8 +363,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         pend = false;
       }
       if (live && it.nsplit > 1) {
-        __threadfence();  // release this CTA's partial (cumulative over the barrier)
-        pend_ticket = atomicAdd(a.counters + it.pair, 1);
+        // releases this CTA's partial (cumulative over the barrier above)
+        pend_ticket = atomic_add_acq_rel_gpu(a.counters + it.pair, 1);
         pend = true;
         pend_b = it.b;
         pend_kvh = it.kvh;
@@ -384,8 +381,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       cit.nsplit = s_flag[3];
       cit.split = cit.p = cit.p_end = cit.ctx = 0;
       __threadfence();  // acquire the other CTAs' partials
-      combine_partials_staged<G, kConsumerWarps * 32>(a, cit, s_flag[4], tid, s_wo,
-                                                      kConsumerWarps * kHeadDim * 8, consumer_sync);
+      if (cit.nsplit <= 4)
+        combine_partials_regs<G, 4>(a, cit, s_flag[4], tid);
+      else
+        combine_partials_staged<G, kConsumerWarps * 32>(a, cit, s_flag[4], tid, s_wo,
+                                                        kConsumerWarps * kHeadDim * 8, consumer_sync);
       if (tid == 0) atomicExch(a.counters + cit.b * a.hkv + cit.kvh, 0);
     }
     const bool more = s_flag[5] != 0;
