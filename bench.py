@@ -163,12 +163,13 @@ def hbm_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(kernel: str, workload: str):
-    """DRAM bytes per launch from the committed ncu summary, if there is one."""
+def profiled_traffic_ratio(kernel: str, workload: str):
+    """DRAM bytes / algorithmic bytes of one launch, from the committed ncu
+    summary of this kernel and workload (None if there is none)."""
     p = REPO / "profiles" / f"{kernel}_{workload}.md"
     if not p.exists():
         return None
-    m = re.search(r"traffic_bytes_per_launch\s*[=:]\s*([0-9.eE+]+)", p.read_text())
+    m = re.search(r"traffic_ratio\s*[=:]\s*([0-9.eE+]+)", p.read_text())
     return float(m.group(1)) if m else None
 
 
@@ -314,7 +315,10 @@ def run_ours(args, rank, world, local):
     achieved = step_bytes / (launch_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "traffic": profiled_traffic("decode_kernel", args.workload),
+                "traffic": (round(ratio * step_bytes) if (ratio := profiled_traffic_ratio("decode_kernel", args.workload))
+                            else None),
+                "traffic_source": (f"ncu dram__bytes_read+write / algorithmic = {ratio} (profiles/decode_kernel_"
+                                   f"{args.workload}.md), times this run's bytes per launch") if ratio else None,
                 "kernel": "decode_kernel", "algorithmic_bytes_per_launch": int(step_bytes),
                 "mean_launch_ms": round(launch_ms, 5)}
 
