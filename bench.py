@@ -57,14 +57,17 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None)
     p.add_argument("--warmup", type=int, default=None)
-    p.add_argument("--workload", default="gqa_b16", choices=["gqa_b16", "mha_b1", "gqa_long", "tp70b"])
+    p.add_argument("--workload", default="gqa_b16",
+                   choices=["gqa_b16", "mha_b1", "gqa_long", "tp70b", "relayout"])
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--cpu-baseline-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--nccl-graph", action="store_true",
+                   help="tp70b at N > 1: capture the step, NCCL all-reduce included, in a CUDA graph")
     return p.parse_args()
 
 
-DEFAULT_STEPS = {"gqa_b16": 20000, "mha_b1": 20000, "gqa_long": 4000, "tp70b": 2000}
+DEFAULT_STEPS = {"gqa_b16": 20000, "mha_b1": 20000, "gqa_long": 4000, "tp70b": 2000, "relayout": 2000}
 
 
 # ----------------------------------------------------------- distributed ----
@@ -252,30 +255,53 @@ def run_ours(args, rank, world, local):
         return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
 
     stream = torch.cuda.Stream(device)
-    graphs, dec_graphs = [], []
+
+    def capture(fns):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for f in fns:
+                f()
+        return g
+
+    # Steps replay from CUDA graphs: one graph holding one step per rotating
+    # input set (so consecutive steps run back to back without a graph launch
+    # in between) plus one single-step graph per set for a remainder.
+    graphed = not (tp and world > 1) or args.nccl_graph
     with torch.cuda.stream(stream):
         for s in sets:  # warm the op once per set before capture
             step(s)
         stream.synchronize()
-        for s in sets:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                decode_only(s)
-            dec_graphs.append(g)
-        if not tp:
-            graphs = dec_graphs
-        elif world == 1:
-            for s in sets:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    step(s)
-                graphs.append(g)
-    replay = (lambda i: graphs[i % n_sets].replay()) if graphs else (lambda i: step(sets[i % n_sets]))
+        dec_multi = capture([lambda s=s: decode_only(s) for s in sets])
+        dec_single = [capture([lambda s=s: decode_only(s)]) for s in sets]
+        if graphed and tp:
+            step_multi = capture([lambda s=s: step(s) for s in sets])
+            step_single = [capture([lambda s=s: step(s)]) for s in sets]
+        elif graphed:
+            step_multi, step_single = dec_multi, dec_single
+
+    def run_steps(multi, single, count, eager=None, events=None):
+        """Runs `count` steps; returns per-launch durations if events are kept."""
+        i, spans = 0, []
+        while i < count:
+            n = n_sets if count - i >= n_sets and (multi is not None) else 1
+            if events is not None:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+            if eager is not None:
+                eager(sets[i % n_sets])
+            elif n == n_sets:
+                multi.replay()
+            else:
+                single[i % n_sets].replay()
+            if events is not None:
+                b.record(stream)
+                spans.append((a, b, n))
+            i += n
+        return spans
 
     with torch.cuda.stream(stream):
-        for i in range(warmup):
-            replay(i)
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        eager_step = None if graphed else step
+        run_steps(step_multi if graphed else None, step_single if graphed else None, warmup, eager_step)
         t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         stream.synchronize()
         barrier(world)
@@ -283,28 +309,26 @@ def run_ours(args, rank, world, local):
         with ClockSampler(local if world > 1 else 0) as clk:
             time.sleep(0.25)  # let the sampler start
             t_all0.record(stream)
-            for i in range(steps):
-                ev[i][0].record(stream)
-                replay(i)
-                ev[i][1].record(stream)
+            spans = run_steps(step_multi if graphed else None, step_single if graphed else None, steps,
+                              eager_step, events=True)
             t_all1.record(stream)
             stream.synchronize()
         torch.cuda.synchronize()
         barrier(world)
     total_ms = max_over_ranks(t_all0.elapsed_time(t_all1), world)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+
+    def per_launch_ms(sp):
+        return sum(a.elapsed_time(b) for a, b, n in sp) / sum(n for _, _, n in sp)
+
+    launch_ms = per_launch_ms(spans)
     if tp:
         # the tp70b step is decode + o_proj (+ all-reduce): time the decode
         # kernel alone for its roofline, replaying its own graphs
         with torch.cuda.stream(stream):
-            for i in range(3):
-                dec_graphs[i % n_sets].replay()
-            for i in range(steps):
-                ev[i][0].record(stream)
-                dec_graphs[i % n_sets].replay()
-                ev[i][1].record(stream)
+            run_steps(dec_multi, dec_single, 3)
+            spans = run_steps(dec_multi, dec_single, steps, events=True)
             stream.synchronize()
-        launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+        launch_ms = per_launch_ms(spans)
     ms_per_step = total_ms / steps
     tokens_per_step = B if tp else B * world
     value = tokens_per_step * steps / (total_ms / 1e3)
@@ -344,7 +368,7 @@ def run_ours(args, rank, world, local):
                    "kv_heads_per_rank": sets[0].k_pool.shape[1],
                    "parallelism": (f"tp{world} (kv-head shards + NCCL all-reduce)" if tp else f"dp{world} (sequence shards)"),
                    "l2": f"{n_sets} rotating input sets, {kv_bytes / 1e6:.1f} MB KV read per step (L2 126 MB)",
-                   "graphs": bool(graphs)},
+                   "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")},
         "kv_gbs": round(kv_bytes / (ms_per_step / 1e3) / 1e9, 1),
         "roofline": roofline,
         "e2e": e2e,
@@ -394,31 +418,166 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
             o = tsb.decode_attention(d["q"], s.k_pool, s.v_pool, d["block_table"], d["context_lens"])
         h_out.copy_(o, non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, warmup // 4)):
-            one()
-        stream.synchronize()
-        barrier(world)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(n):
-            one()
-        b.record(stream)
-        stream.synchronize()
-    ms = max_over_ranks(a.elapsed_time(b), world) / n
+    def timed(run):
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, warmup // 4)):
+                run()
+            stream.synchronize()
+            barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(n):
+                run()
+            b.record(stream)
+            stream.synchronize()
+        return max_over_ranks(a.elapsed_time(b), world) / n
+
+    eager_ms = timed(one)
+    graph_ms = None
+    if not (tp and world > 1):
+        # the same public-API step captured once and replayed per step: every
+        # replay performs the host->device copies, the append, the decode and
+        # the device->host copy of that step
+        with torch.cuda.stream(stream):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                one()
+        graph_ms = timed(g.replay)
+    ms = graph_ms if graph_ms is not None else eager_ms
     tokens = B if tp else B * world
     return {"value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms, 5),
-            "path": "torch.ops.b200kv.kv_append + decode_attention, pinned host buffers"}
+            "path": ("torch.ops.b200kv.kv_append + decode_attention with pinned host buffers, "
+                     + ("captured once in a CUDA graph and replayed per step" if graph_ms is not None
+                        else "eager")),
+            "eager": {"value": round(tokens / (eager_ms / 1e3), 1), "ms_per_step": round(eager_ms, 5)}}
+
+
+# --------------------------------------------------------------- relayout ----
+def run_relayout(args, rank, world, local):
+    """append 64 tokens x 8 KV heads into random slots, then
+    relayout a 131072 x 8 x 128 fp16 row-major cache into 64-token stick pages
+    and back.  Metric: bytes moved per second (each byte read or written once)."""
+    import torch_spyre_b200 as tsb
+    from torch_spyre_b200.workloads import RELAYOUT_CONFIG, seeded_generator
+
+    cfg = RELAYOUT_CONFIG
+    device = torch.device("cuda", local if world > 1 else 0)
+    steps = args.steps or DEFAULT_STEPS["relayout"]
+    warmup = max(3, args.warmup if args.warmup is not None else 20)
+    T, hkv, D = cfg.bulk_tokens, cfg.num_kv_heads, cfg.head_dim
+    g = seeded_generator("relayout", "bulk", rank, device="cuda")
+    rows = torch.randn((T, hkv, D), generator=g, device=device, dtype=torch.float16)
+    nb = 2 * T // 64
+    ids = torch.randperm(nb, generator=seeded_generator("relayout", "ids", rank))[: T // 64].to(torch.int32).to(device)
+    pool_k = torch.zeros((nb, hkv, D // 64, 64, 64), dtype=torch.float16, device=device)
+    pool_v = torch.zeros_like(pool_k)
+    n = cfg.append_tokens
+    slots = torch.randperm(nb * 64, generator=seeded_generator("relayout", "slots", rank))[:n].to(device)
+    k_new = torch.randn((n, hkv, D), device=device, dtype=torch.float16)
+    v_new = torch.randn_like(k_new)
+    bulk = T * hkv * D * 2
+    step_bytes = 2 * 2 * bulk + 2 * 2 * n * hkv * D * 2  # relayout there and back + append K/V
+
+    stream = torch.cuda.Stream(device)
+
+    def step():
+        tsb.kv_append(k_new, v_new, pool_k, pool_v, slots)
+        tsb.kv_relayout(rows, pool_k, ids)
+        return tsb.kv_unrelayout(pool_k, ids, T)
+
+    with torch.cuda.stream(stream):
+        back = step()
+        stream.synchronize()
+        assert torch.equal(back.view(torch.int16), rows.view(torch.int16))
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            step()
+        for _ in range(warmup):
+            gr.replay()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        barrier(world)
+        with ClockSampler(local if world > 1 else 0) as clk:
+            time.sleep(0.25)
+            t0.record(stream)
+            for i in range(steps):
+                ev[i][0].record(stream)
+                gr.replay()
+                ev[i][1].record(stream)
+            t1.record(stream)
+            stream.synchronize()
+        barrier(world)
+    total_ms = max_over_ranks(t0.elapsed_time(t1), world)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    peak, kind = hbm_peak()
+    achieved = step_bytes / (launch_ms / 1e3) / 1e9
+    line = {
+        "metric": "KV relayout/append bytes moved per second", "value": round(step_bytes * world * steps / total_ms / 1e6, 1),
+        "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": round(total_ms / steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 (bit copy)", "data": "synthetic (seeded N(0,1) fp16)",
+        "config": {"workload": "relayout", "bulk_tokens": T, "num_kv_heads": hkv, "head_dim": D,
+                   "append_tokens": n, "l2": f"{2 * bulk / 1e6:.0f} MB per direction > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": kind, "traffic": None,
+                     "kernel": "kv_append + relayout_kernel<0> + relayout_kernel<1> (one step)",
+                     "algorithmic_bytes_per_launch": step_bytes, "mean_launch_ms": round(launch_ms, 5)},
+        "gpu_launches": 3 * steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------- reference ----
+def run_reference_relayout(args):
+    """The oracle's append + relayout (numpy, host) on a bounded slice of the cache."""
+    import numpy as np
+
+    from oracle import kv_relayout as okv
+    from torch_spyre_b200.workloads import RELAYOUT_CONFIG
+
+    cfg = RELAYOUT_CONFIG
+    steps = args.steps or DEFAULT_STEPS["relayout"]
+    warmup = max(3, args.warmup if args.warmup is not None else 20)
+    budget = min(1.0, max(0.002, 120.0 / (steps + warmup)))
+    rng = np.random.default_rng(0)
+    T = 64 * 64
+    rows = rng.standard_normal((T, cfg.num_kv_heads, cfg.head_dim)).astype(np.float16)
+    ids = np.arange(T // 64, dtype=np.int32)[::-1].copy()
+    pool = np.zeros((T // 64, cfg.num_kv_heads, cfg.head_dim // 64, 64, 64), np.float16)
+    t0 = time.perf_counter()
+    okv.pool_to_rows(okv.rows_to_pool(rows, pool, ids), ids, T)
+    per = time.perf_counter() - t0
+    reps = max(1, int(budget / max(per, 1e-9)))
+    bytes_per_rep = 4 * rows.nbytes
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            okv.pool_to_rows(okv.rows_to_pool(rows, pool, ids), ids, T)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    value = bytes_per_rep * reps * steps / sum(times) / 1e9
+    line = {"impl": "reference", "metric": "KV relayout/append bytes moved per second", "value": round(value, 3),
+            "unit": "GB/s", "n_gpus": 1, "steps": steps, "warmup": warmup, "higher_is_better": True,
+            "config": {"workload": "relayout"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": f"{reps} x relayout of 4096 tokens there and back per step (numpy oracle)"},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, rank, world):
     """The reference's CPU eager decode path on the host cores (rank 0 only)."""
     if rank != 0:
         return
     from torch_spyre_b200.workloads import DECODE_CONFIGS, make_decode_inputs
 
+    if args.workload == "relayout":
+        return run_reference_relayout(args)
     cfg = DECODE_CONFIGS[args.workload]
     steps = args.steps or DEFAULT_STEPS[args.workload]
     warmup = max(3, args.warmup if args.warmup is not None else 20)
@@ -467,7 +626,10 @@ def main():
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        run_ours(args, rank, world, local)
+        if args.workload == "relayout":
+            run_relayout(args, rank, world, local)
+        else:
+            run_ours(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist
