@@ -119,13 +119,15 @@ B200KV_API int64_t b200kv_decode_workspace_bytes(int64_t batch, int64_t num_q_he
  * lse          optional fp32 [batch, num_q_heads] (natural-log logsumexp of the
  *              scaled scores; -inf for an empty context), may be NULL
  * scale        softmax scale (the reference default is 1/sqrt(D))
- * num_splits   0 = automatic: the KV stream of the whole batch is cut into one
- *              equal partition per SM; n > 0 = n equal partitions (n <= 8192).
- *              A sequence-head cut by a partition boundary is a split whose
- *              partials are merged with a log-sum-exp combine.
+ * num_splits   0 = automatic: one partition (CTA) per SM; n > 0 = n partitions
+ *              (n <= 1024).  The KV pages of the whole batch are cut into equal
+ *              contiguous shares, one per partition; a sequence-head cut by a
+ *              share boundary is a split whose partials are merged with a
+ *              log-sum-exp combine.
  * workspace    device buffer of at least b200kv_decode_workspace_bytes()
  * error_flag   optional device int32 (B200KV_DEVERR_* bits are OR-ed in)
- * Supported: head_dim 128, Hq % Hkv == 0, Hq / Hkv in {1, 2, 4, 8}, batch <= 1024.
+ * Supported: head_dim 128, Hq % Hkv == 0, Hq / Hkv in {1, 2, 4, 8}, batch <= 1024,
+ * batch * Hkv <= 131072.
  * An empty context (len 0) yields a zero output row, matching torch CPU SDPA.
  */
 B200KV_API int b200kv_decode_attention_f16(

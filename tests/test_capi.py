@@ -61,7 +61,7 @@ def _decode(**over):
     (dict(q=None), 1, "null"),
     (dict(q=(1 << 20) + 2), 1, "aligned"),
     (dict(bts=2), 1, "block_table_stride"),
-    (dict(splits=8193), 1, "num_splits"),
+    (dict(splits=1025), 1, "num_splits"),
     (dict(B=2000), 2, "batch"),
     (dict(scale=float("nan")), 1, "scale"),
     (dict(), 3, "workspace"),

@@ -140,15 +140,6 @@ __device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint
       : "memory");
 }
 
-// atomicAdd with acquire-release semantics at GPU scope.  A thread that takes
-// a CTA barrier after its CTA's stores and then calls this releases those
-// stores (cumulativity) and acquires what earlier releasers published.
-__device__ __forceinline__ int atomic_add_acq_rel_gpu(int *addr, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
-  return old;
-}
-
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

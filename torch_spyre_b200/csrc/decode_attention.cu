@@ -74,8 +74,8 @@ extern "C" int b200kv_decode_attention_f16(
   B200KV_CHECK_ARG(num_blocks > 0 && max_blocks_per_seq > 0, "num_blocks and max_blocks_per_seq must be > 0");
   B200KV_CHECK_ARG(max_blocks_per_seq * kPageTokens < (int64_t{1} << 31), "max_blocks_per_seq too large");
   B200KV_CHECK_ARG(block_table_stride >= max_blocks_per_seq, "block_table_stride < max_blocks_per_seq");
-  B200KV_CHECK_ARG(num_splits >= 0 && num_splits <= kMaxWorkItems, "num_splits must be in [0, %d]",
-                   kMaxWorkItems);
+  B200KV_CHECK_ARG(num_splits >= 0 && num_splits <= kMaxPartitions, "num_splits must be in [0, %d]",
+                   kMaxPartitions);
   if (batch * num_kv_heads * max_blocks_per_seq >= (int64_t{1} << 31))
     return set_error(B200KV_ERR_UNSUPPORTED, "batch * num_kv_heads * max_blocks_per_seq >= 2^31");
   B200KV_CHECK_ARG(std::isfinite(scale), "scale must be finite");

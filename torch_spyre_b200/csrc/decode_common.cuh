@@ -10,7 +10,8 @@
 namespace b200kv {
 
 constexpr int kMaxBatch = 1024;
-constexpr int kMaxWorkItems = 8192;
+constexpr int kMaxWorkItems = 1024;   // partial slots beyond one per pair
+constexpr int kMaxPartitions = 1024;  // CTAs of a decode launch (one slot each)
 constexpr int kDefaultItemsPerCta = 4;
 // The completion counters always occupy the same fixed-size region at the
 // start of the workspace, whatever the call's shape, so a workspace shared by
@@ -249,38 +250,74 @@ __device__ __forceinline__ void build_unit_plan(const DecodeArgs &a, Plan &p) {
   p.chunk = 0;
 }
 
-struct Seg {
+// The partition of one launch over `grid` CTAs ("stream-K"): CTA c streams
+// the units [c * per, (c + 1) * per), per = ceil(units / grid), so every CTA
+// streams the same number of pages whatever the spread of context lengths.
+// A pair cut by a CTA boundary is a split: its piece in CTA c writes slot
+// pair + c.  Along the unit stream pair and c never decrease and each new
+// piece increases one of them, so slots are unique and a pair's pieces occupy
+// the contiguous slots pair + c_lo .. pair + c_hi.
+struct Partition {
+  int units, grid, per;
+  __device__ __forceinline__ int lo(int c) const { return min(c * per, units); }
+  __device__ __forceinline__ int hi(int c) const { return min((c + 1) * per, units); }
+};
+
+__device__ __forceinline__ Partition make_partition(int units, int grid) {
+  Partition P;
+  P.units = units;
+  P.grid = grid;
+  P.per = max(1, (units + grid - 1) / grid);
+  return P;
+}
+
+struct SlotMap {
+  int first, count;
+  __device__ __forceinline__ int n() const { return count; }
+  __device__ __forceinline__ int operator()(int s) const { return first + s; }
+};
+
+__device__ __forceinline__ SlotMap pair_slots(const Partition &P, int pair, int pj, int w) {
+  const int c_lo = pj / P.per, c_hi = (pj + w - 1) / P.per;
+  return SlotMap{pair + c_lo, c_hi - c_lo + 1};
+}
+
+// First unit and unit count of a pair.
+__device__ __forceinline__ void pair_units(const DecodeArgs &a, const Plan &pl, int pair, int *pj,
+                                           int *w) {
+  const int b = pair / a.hkv, kvh = pair - (pair / a.hkv) * a.hkv;
+  *w = max(pl.nb[b], 1);
+  *pj = a.hkv * pl.prefix[b] + kvh * *w;
+}
+
+struct Piece {
   int b, kvh, pair;     // sequence, KV head, pair index b * Hkv + kvh
   int p, p_end, ctx;    // pages [p, p_end) of the pair streamed by this piece
-  int nsplit, split;    // pieces of the pair, index of this one
-  int first_slot, slot; // partial slots: pair's first, this piece's
+  int nsplit, slot;     // pieces of the pair, this piece's partial slot
   int u_next;           // first unit after this piece
 };
 
-// The piece of work that starts at unit u inside CTA c's range [.., u_end).
-__device__ __forceinline__ Seg locate_seg(const DecodeArgs &a, const Plan &pl, int u, int u_end,
-                                          int c, int per) {
+// The piece that starts at unit u of CTA c's range, which ends at u_hi.
+__device__ __forceinline__ Piece locate_piece(const DecodeArgs &a, const Plan &pl,
+                                              const Partition &P, int u, int u_hi, int c) {
   int lo = 0, hi = a.batch - 1;  // largest b whose first unit is <= u
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (a.hkv * pl.prefix[mid] <= u) lo = mid; else hi = mid - 1;
   }
-  Seg s;
+  Piece s;
   s.b = lo;
   const int nb = pl.nb[lo];
   const int w = max(nb, 1);
   const int base = a.hkv * pl.prefix[lo];
   s.kvh = (u - base) / w;
   const int pj = base + s.kvh * w;  // first unit of the pair
-  const int hi_u = min(u_end, pj + w);
+  const int hi_u = min(u_hi, pj + w);
   s.pair = lo * a.hkv + s.kvh;
   s.p = min(u - pj, nb);
   s.p_end = min(hi_u - pj, nb);
   s.ctx = pl.ctx[lo];
-  const int c_lo = pj / per, c_hi = (pj + w - 1) / per;
-  s.nsplit = c_hi - c_lo + 1;
-  s.split = c - c_lo;
-  s.first_slot = s.pair + c_lo;
+  s.nsplit = pair_slots(P, s.pair, pj, w).n();
   s.slot = s.pair + c;
   s.u_next = hi_u;
   return s;
@@ -310,128 +347,81 @@ __device__ __forceinline__ void store_lse(const DecodeArgs &a, int b, int h, flo
 // Log-sum-exp merge of the nsplit partials of (b, kv head), run by the CTA
 // that finished last.  Threads [0, NT) cover the G x 128 outputs.
 template <int G, int NT>
-__device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item &it, int first,
-                                                 int tid) {
+__device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item &it,
+                                                 const SlotMap &sm, int tid) {
   const int h0 = it.kvh * G;
   for (int i = tid; i < G * kHeadDim; i += NT) {
     const int g = i / kHeadDim, d = i % kHeadDim;
     float mx = -CUDART_INF_F;
     for (int s = 0; s < it.nsplit; ++s)
-      mx = fmaxf(mx, __ldcg(a.part_ml + static_cast<int64_t>(first + s) * G + g).x);
+      mx = fmaxf(mx, __ldcg(a.part_ml + static_cast<int64_t>(sm(s)) * G + g).x);
     float lsum = 0.f, acc = 0.f;
     for (int s = 0; s < it.nsplit; ++s) {
-      const float2 ml = __ldcg(a.part_ml + static_cast<int64_t>(first + s) * G + g);
+      const float2 ml = __ldcg(a.part_ml + static_cast<int64_t>(sm(s)) * G + g);
       const float w = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - mx);
       lsum = fmaf(ml.y, w, lsum);
-      acc = fmaf(__ldcg(a.part_o + static_cast<int64_t>(first + s) * G * kHeadDim + i), w, acc);
+      acc = fmaf(__ldcg(a.part_o + static_cast<int64_t>(sm(s)) * G * kHeadDim + i), w, acc);
     }
     store_out(a, it.b, h0 + g, d, acc, lsum);
     if (d == 0) store_lse(a, it.b, h0 + g, mx, lsum);
   }
 }
 
-// Merge of at most MAXS partials by 128 threads, thread d producing output dim
-// d of every head: all partial loads are issued before any is used, so the
-// merge costs one memory round trip and no barrier.
-template <int G, int MAXS>
-__device__ __forceinline__ void combine_partials_regs(const DecodeArgs &a, const Item &it,
-                                                      int first, int d) {
-  const int ns = it.nsplit;
-  float2 ml[MAXS][G];
-  float ov[MAXS][G];
-  const float2 *mls = a.part_ml + static_cast<int64_t>(first) * G;
-  const float *po = a.part_o + static_cast<int64_t>(first) * G * kHeadDim + d;
-#pragma unroll
-  for (int s = 0; s < MAXS; ++s)
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const bool in = s < ns;
-      ml[s][g] = in ? __ldcg(mls + s * G + g) : make_float2(-CUDART_INF_F, 0.f);
-      ov[s][g] = in ? __ldcg(po + (s * G + g) * kHeadDim) : 0.f;
-    }
-  const int h0 = it.kvh * G;
+// Log-sum-exp merge of a pair's split partials by one warp: lane l produces
+// output dims l, l + 32, l + 64, l + 96 of every head of the pair.  Splits are
+// read two at a time (every load of a batch issued before any is used) and
+// folded into a running (max, sum, accumulator) per head, so any number of
+// splits merges without shared memory.
+template <int G>
+__device__ __forceinline__ void combine_online_warp(const DecodeArgs &a, int b, int kvh,
+                                                    const SlotMap &sm, int lane) {
+  float M[G], Ls[G], acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float mx = -CUDART_INF_F;
+    M[g] = -CUDART_INF_F;
+    Ls[g] = 0.f;
 #pragma unroll
-    for (int s = 0; s < MAXS; ++s) mx = fmaxf(mx, ml[s][g].x);
-    float l = 0.f, acc = 0.f;
+    for (int k = 0; k < 4; ++k) acc[g][k] = 0.f;
+  }
+  const int ns = sm.n();
+  for (int s0 = 0; s0 < ns; s0 += 2) {
+    float2 ml[2][G];
+    float ov[2][G][4];
 #pragma unroll
-    for (int s = 0; s < MAXS; ++s) {
-      const float w = ml[s][g].x == -CUDART_INF_F ? 0.f : exp2f(ml[s][g].x - mx);
-      l = fmaf(ml[s][g].y, w, l);
-      acc = fmaf(ov[s][g], w, acc);
+    for (int j = 0; j < 2; ++j) {
+      const bool in = s0 + j < ns;
+      const int64_t slot = sm(in ? s0 + j : s0);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        ml[j][g] = in ? __ldcg(a.part_ml + slot * G + g) : make_float2(-CUDART_INF_F, 0.f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ov[j][g][k] = in ? __ldcg(a.part_o + (slot * G + g) * kHeadDim + lane + 32 * k) : 0.f;
+      }
     }
-    store_out(a, it.b, h0 + g, d, acc, l);
-    if (d == 0) store_lse(a, it.b, h0 + g, mx, l);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float m = ml[j][g].x;
+        if (m != -CUDART_INF_F) {
+          const float mn = fmaxf(M[g], m);
+          const float w_old = M[g] == -CUDART_INF_F ? 0.f : exp2f(M[g] - mn);
+          const float w_new = exp2f(m - mn);
+          Ls[g] = Ls[g] * w_old + ml[j][g].y * w_new;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) acc[g][k] = acc[g][k] * w_old + ov[j][g][k] * w_new;
+          M[g] = mn;
+        }
+      }
   }
-}
-
-// Same merge with the split weights staged in shared memory (`scratch`,
-// capacity `cap` floats, shared by the NT threads, which must all call this):
-// the per-split max/sum are read once, each thread then streams its partial
-// outputs with independent, unrolled loads.  Falls back to combine_partials
-// when the splits do not fit.
-template <int G, int NT, typename SyncFn>
-__device__ __forceinline__ void combine_partials_staged(const DecodeArgs &a, const Item &it,
-                                                        int first, int tid, float *scratch,
-                                                        int cap, SyncFn sync) {
-  const int ns = it.nsplit;
-  if (3 * ns * G + 2 * G > cap) {
-    combine_partials<G, NT>(a, it, first, tid);
-    return;
+  const int h0 = kvh * G;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) store_out(a, b, h0 + g, lane + 32 * k, acc[g][k], Ls[g]);
+    if (lane == 0) store_lse(a, b, h0 + g, M[g], Ls[g]);
   }
-  float *w = scratch;                 // [ns][G] weights exp2(m_s - M) / L
-  float *stat = scratch + ns * G;     // M[G], L[G]
-  float *mls = stat + 2 * G;          // [ns][G] (m, l) pairs
-  const float2 *src = a.part_ml + static_cast<int64_t>(first) * G;
-  for (int i = tid; i < ns * G; i += NT) {
-    const float2 ml = __ldcg(src + i);
-    mls[2 * i] = ml.x;
-    mls[2 * i + 1] = ml.y;
-  }
-  sync();
-  if (tid < G) {
-    float mx = -CUDART_INF_F;
-    for (int s = 0; s < ns; ++s) mx = fmaxf(mx, mls[2 * (s * G + tid)]);
-    float l = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float m = mls[2 * (s * G + tid)];
-      l = fmaf(mls[2 * (s * G + tid) + 1], m == -CUDART_INF_F ? 0.f : exp2f(m - mx), l);
-    }
-    stat[tid] = mx;
-    stat[G + tid] = l;
-  }
-  sync();
-  for (int i = tid; i < ns * G; i += NT) {
-    const int g = i % G;
-    const float m = mls[2 * i], mx = stat[g], l = stat[G + g];
-    w[i] = (m == -CUDART_INF_F || !(l > 0.f)) ? 0.f : exp2f(m - mx) / l;
-  }
-  sync();
-  const int h0 = it.kvh * G;
-  for (int i = tid; i < G * kHeadDim; i += NT) {
-    const int g = i / kHeadDim, d = i % kHeadDim;
-    const float *po = a.part_o + static_cast<int64_t>(first) * G * kHeadDim + i;
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-    int s = 0;
-    for (; s + 4 <= ns; s += 4) {
-      const float v0 = __ldcg(po + (s + 0) * G * kHeadDim);
-      const float v1 = __ldcg(po + (s + 1) * G * kHeadDim);
-      const float v2 = __ldcg(po + (s + 2) * G * kHeadDim);
-      const float v3 = __ldcg(po + (s + 3) * G * kHeadDim);
-      acc0 = fmaf(v0, w[(s + 0) * G + g], acc0);
-      acc1 = fmaf(v1, w[(s + 1) * G + g], acc1);
-      acc2 = fmaf(v2, w[(s + 2) * G + g], acc2);
-      acc3 = fmaf(v3, w[(s + 3) * G + g], acc3);
-    }
-    for (; s < ns; ++s) acc0 = fmaf(__ldcg(po + s * G * kHeadDim), w[s * G + g], acc0);
-    const float l = stat[G + g];
-    a.out[it.b * a.o_sb + (h0 + g) * a.o_sh + d] =
-        __float2half_rn(l > 0.f ? (acc0 + acc1) + (acc2 + acc3) : 0.f);
-    if (d == 0) store_lse(a, it.b, h0 + g, stat[g], l);
-  }
-  sync();
 }
 
 }  // namespace b200kv

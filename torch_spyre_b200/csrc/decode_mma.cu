@@ -9,52 +9,77 @@
 // in the n = 8 dimension (G < 8 is zero-padded), which leaves the SMs almost
 // idle and the kernel bound by HBM.
 //
-// CTA = 1 producer warp + 4 consumer warps, one CTA per SM (persistent):
-// Work partition: the balanced unit split of decode_common.cuh (every CTA
-// streams the same number of pages; a sequence-head cut by a CTA boundary is
-// a split).
-//   producer  walks this CTA's pieces page by page: block ids are fetched
-//             32 at a time by the whole warp, the piece's q rows are staged
-//             with its first page, and lane 0 issues two 3-D TMA loads per page (K, V;
-//             16 KiB each, 128-byte swizzle, L2 evict-first) into an NST-stage
-//             ring, waiting on each stage's "empty" mbarrier and arming its
-//             "full" mbarrier with the bytes;
-//   consumer  warp w owns tokens [16w, 16w + 16) of every page and keeps its
+// CTA = 1 producer warp + 4 consumer warps + 1 epilogue warp, one CTA per SM
+// (persistent).  Work partition: the balanced unit split of decode_common.cuh
+// (every CTA streams the same number of pages; a sequence-head cut by a CTA
+// boundary is a split).
+//   producer  walks this CTA's pieces page by page: block ids are fetched 32 at
+//             a time by the whole warp; lane 0 writes a small descriptor per
+//             stage (piece, page, flags), issues two 3-D TMA loads per page
+//             (K, V; 16 KiB each, 128-byte swizzle, L2 evict-first) and, with
+//             the first page of a piece, one bulk copy per q row, into an
+//             NST-stage ring with "full"/"empty" mbarriers;
+//   consumers warp w owns tokens [16w, 16w + 16) of every page and keeps its
 //             own online-softmax state, so no CTA barrier is taken per page:
 //               S^T[16 t x 8 h] = K[16 t x 128 d] . Q^T   (8 mma, ldmatrix)
 //               mask t >= ctx, exp2-domain online softmax (shuffles over t)
 //               P^T fragment from S^T by movmatrix.trans
 //               O^T[128 d x 8 h] += V^T[128 d x 16 t] . P^T (8 mma, ldmatrix.trans)
-//             then one arrive on the stage's empty barrier.
-// At the end of a piece the 4 warps' (m, l, O) are merged in shared
-// memory; a single split writes the fp16 output, otherwise the unnormalised
-// partial goes to the workspace and the CTA that takes the last ticket of the
-// (b, kv head) merges all partials (decode_common.cuh); the ticket is read one
-// piece later so its atomic round trip overlaps useful work.
+//             then one arrive on the stage's empty barrier; at the end of a
+//             piece each warp drops its state into one of two piece buffers
+//             and goes on with the next page;
+//   epilogue  merges the 4 warps' states of a finished piece, writes the fp16
+//             output (unsplit pair) or the fp32 partial, takes the pair's
+//             completion ticket and, holding the last one, merges the pair's
+//             partials (online log-sum-exp, decode_common.cuh).
 #include "decode_kernels.h"
 
 namespace b200kv {
 namespace {
 
 constexpr int kConsumerWarps = 4;
-constexpr int kMmaThreads = (kConsumerWarps + 1) * 32;
+constexpr int kProducerWarp = kConsumerWarps;      // warp 4
+constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warp 5
+constexpr int kMmaThreads = (kConsumerWarps + 2) * 32;
 
 // Staged q of one piece: G rows of 128 fp16, row stride padded to 272 B so
 // the Q^T fragment loads (8 heads x 4 lanes) hit 32 distinct banks.
 constexpr int kQRowBytes = 272;
 constexpr int kQSlotBytes = 8 * kQRowBytes;
 
+// Hand-off of a finished piece from the consumer warps to the epilogue warp:
+// every warp's unnormalised O^T [128 d][8 h], its (max, sum) per head and the
+// piece's identity.  Two buffers let the consumers run a piece ahead.
+struct PieceHeader {
+  int b, kvh, pair, nsplit, slot, end;
+};
+constexpr int kPieceO = 0;                                   // float [4][128][8]
+constexpr int kPieceML = kConsumerWarps * kHeadDim * 8 * 4;  // float2 [4][8]
+constexpr int kPieceHdr = kPieceML + kConsumerWarps * 8 * 8;
+constexpr int kPieceBytes = (kPieceHdr + 64 + 127) & ~127;
+constexpr int kPieceBufs = 2;
+
 template <int NST>
 struct MmaSmem {
   static constexpr int kStageBytes = 2 * kPageBytes;                     // K page + V page
   static constexpr int kQ = NST * kStageBytes;                           // q slot per stage
-  static constexpr int kWO = kQ + NST * kQSlotBytes;                     // float [4][128][8]
-  static constexpr int kWML = kWO + kConsumerWarps * kHeadDim * 8 * 4;   // float2 [4][8]
-  static constexpr int kPlan = kWML + kConsumerWarps * 8 * 8;
-  static constexpr int kBars = (kPlan + kPlanBytes + 7) & ~7;            // full[NST], empty[NST]
-  static constexpr int kBytes = kBars + 2 * NST * 8;
+  static constexpr int kPiece = kQ + NST * kQSlotBytes;                  // piece buffers
+  static constexpr int kDesc = kPiece + kPieceBufs * kPieceBytes;        // StageDesc [NST]
+  static constexpr int kPlan = kDesc + NST * 32;
+  static constexpr int kBars = (kPlan + kPlanBytes + 7) & ~7;  // full, empty [NST]; pfull, pempty [2]
+  static constexpr int kBytes = kBars + (2 * NST + 2 * kPieceBufs) * 8;
   static constexpr int kAlloc = kBytes + 1024;
 };
+
+// What one stage carries, written by the producer before it arms the stage's
+// full barrier: the piece (pair, slot, split count), the page and flags.
+struct StageDesc {
+  int b, kvh, pair, page, ctx, nsplit, slot, flags;
+};
+constexpr int kDescFirst = 1;  // first page of a piece
+constexpr int kDescLast = 2;   // last page of a piece
+constexpr int kDescPage = 4;   // the stage holds a page (an empty sequence has none)
+constexpr int kDescEnd = 8;    // no more work for this CTA
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -86,9 +111,6 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -115,10 +137,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float *s_wo = reinterpret_cast<float *>(smem + L::kWO);
-  float2 *s_wml = reinterpret_cast<float2 *>(smem + L::kWML);
+  StageDesc *descs = reinterpret_cast<StageDesc *>(smem + L::kDesc);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::kBars);
   uint64_t *empty = full + NST;
+  uint64_t *pfull = empty + NST;         // piece handed to the epilogue (4 arrivals)
+  uint64_t *pempty = pfull + kPieceBufs; // piece buffer free again (1 arrival)
   Plan pl = plan_view(smem + L::kPlan);
 
   const int tid = threadIdx.x;
@@ -132,52 +155,161 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    for (int s = 0; s < kPieceBufs; ++s) {
+      mbar_init(&pfull[s], kConsumerWarps);
+      mbar_init(&pempty[s], 1);
+    }
     fence_mbar_init();
   }
+  // Programmatic dependent launch: nothing above reads global memory; wait for
+  // the preceding grid on the stream to finish (a no-op when this launch has
+  // no programmatic predecessor), then let the next grid be scheduled so its
+  // CTAs take over SMs as soon as ours exit.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   build_unit_plan<kMmaThreads>(a, pl);  // synchronises the CTA
-  const int total_units = pl.total_items;
-  const int per = max(1, (total_units + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x));
+  const Partition P = make_partition(pl.total_items, static_cast<int>(gridDim.x));
   const int c = blockIdx.x;
-  const int u_begin = min(c * per, total_units);
-  const int u_end = min(u_begin + per, total_units);
 
   // ------------------------------------------------------------ producer --
-  // The whole warp fetches the next 32 block ids of a piece in one coalesced
-  // load (so page issue never waits on a block-table read); lane 0 arms the
-  // stage's full barrier and issues the two page loads, plus, with the first
-  // page of a piece, one bulk copy per q row into the stage's q slot.
-  if (warp == kConsumerWarps) {
+  // Streams this CTA's range of units.  Per page: the whole warp fetches block ids 32 at
+  // a time in one coalesced load; lane 0 waits for the stage to be free,
+  // writes its descriptor, arms its full barrier and issues the two page
+  // loads, plus, with the first page of a piece, one bulk copy per q row.
+  if (warp == kProducerWarp) {
     const uint64_t policy = l2_policy_evict_first();
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = u_begin; u < u_end;) {
-      const Seg it = locate_seg(a, pl, u, u_end, c, per);
-      u = it.u_next;
-      for (int base = it.p; base < it.p_end; base += 32) {
-        const int n = min(32, it.p_end - base);
-        const int my_blk = lane < n ? page_block(a, it.b, base + lane) : 0;
-        for (int j = 0; j < n; ++j) {
-          const int blk = __shfl_sync(0xffffffffu, my_blk, j);
-          if (lane == 0) {
-            mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
-            const int page = blk * a.hkv + it.kvh;
-            uint8_t *dst = smem + stage * L::kStageBytes;
-            const bool first = base + j == it.p;
-            mbar_arrive_expect_tx(&full[stage], 2 * kPageBytes + (first ? G * kHeadDim * 2 : 0));
-            if (first) {  // the piece's q rows ride on its first page's barrier
-              uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
-              const __half *qg = a.q + it.b * a.q_sb + (it.kvh * G) * a.q_sh;
+    auto emit_range = [&](int u_lo, int u_hi, int owner) {
+      for (int u = u_lo; u < u_hi;) {
+        const Piece pc = locate_piece(a, pl, P, u, u_hi, owner);
+        u = pc.u_next;
+        const int npages = pc.p_end - pc.p;
+        const int nstages = max(npages, 1);  // an empty sequence still takes one stage
+        for (int base = 0; base < nstages; base += 32) {
+          const int n = min(32, nstages - base);
+          const int my_blk = (lane < n && npages > 0) ? page_block(a, pc.b, pc.p + base + lane) : 0;
+          for (int j = 0; j < n; ++j) {
+            const int blk = __shfl_sync(0xffffffffu, my_blk, j);
+            if (lane == 0) {
+              mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
+              const int i = base + j;
+              const bool has = npages > 0;
+              StageDesc &d = descs[stage];
+              d.b = pc.b;
+              d.kvh = pc.kvh;
+              d.pair = pc.pair;
+              d.page = pc.p + i;
+              d.ctx = pc.ctx;
+              d.nsplit = pc.nsplit;
+              d.slot = pc.slot;
+              d.flags = (i == 0 ? kDescFirst : 0) | (i == nstages - 1 ? kDescLast : 0) |
+                        (has ? kDescPage : 0);
+              uint32_t tx = has ? 2 * kPageBytes : 0;
+              if (has && i == 0) tx += G * kHeadDim * 2;
+              mbar_arrive_expect_tx(&full[stage], tx);
+              if (has) {
+                if (i == 0) {  // the piece's q rows ride on its first page's barrier
+                  uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
+                  const __half *qg = a.q + pc.b * a.q_sb + (pc.kvh * G) * a.q_sh;
 #pragma unroll
-              for (int g = 0; g < G; ++g) bulk_load(qs + g * kQRowBytes, qg + g * a.q_sh, kHeadDim * 2, &full[stage]);
+                  for (int g = 0; g < G; ++g)
+                    bulk_load(qs + g * kQRowBytes, qg + g * a.q_sh, kHeadDim * 2, &full[stage]);
+                }
+                uint8_t *dst = smem + stage * L::kStageBytes;
+                const int page = blk * a.hkv + pc.kvh;
+                tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
+                tma_load_3d(dst + kPageBytes, &vmap, &full[stage], 0, 0, page, policy);
+              }
             }
-            tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
-            tma_load_3d(dst + kPageBytes, &vmap, &full[stage], 0, 0, page, policy);
-          }
-          if (++stage == NST) {
-            stage = 0;
-            phase ^= 1u;
+            if (++stage == NST) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
+      }
+    };
+    emit_range(P.lo(c), P.hi(c), c);
+    if (lane == 0) {  // end marker
+      mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
+      descs[stage].flags = kDescEnd;
+      mbar_arrive_expect_tx(&full[stage], 0);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ epilogue --
+  // Takes finished pieces from the consumers: merges the 4 warps' states,
+  // writes the fp16 output (single piece) or the fp32 partial, takes the
+  // pair's completion ticket and, holding the last one, merges the pair's
+  // partials.  Runs beside the consumers, which never wait for it unless it
+  // falls two pieces behind.
+  if (warp == kEpilogueWarp) {
+    for (int k = 0;; ++k) {
+      const int pb = k & 1;
+      mbar_wait_bounded(&pfull[pb], (k >> 1) & 1, a.error_flag);
+      const uint8_t *buf = smem + L::kPiece + pb * kPieceBytes;
+      const PieceHeader hd = *reinterpret_cast<const PieceHeader *>(buf + kPieceHdr);
+      if (hd.end) break;
+      const float *wo = reinterpret_cast<const float *>(buf + kPieceO);
+      const float2 *wml = reinterpret_cast<const float2 *>(buf + kPieceML);
+      float acc[G][4], mx[G], ls[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float m = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, wml[w * 8 + g].x);
+        float l = 0.f, sw[kConsumerWarps];
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float2 ml = wml[w * 8 + g];
+          sw[w] = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - m);
+          l = fmaf(ml.y, sw[w], l);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          float x = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w)
+            x = fmaf(wo[(w * kHeadDim + lane + 32 * kk) * 8 + g], sw[w], x);
+          acc[g][kk] = x;
+        }
+        mx[g] = m;
+        ls[g] = l;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[pb]);  // buffer read: the consumers may refill it
+      const int h0 = hd.kvh * G;
+      if (hd.nsplit == 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) store_out(a, hd.b, h0 + g, lane + 32 * kk, acc[g][kk], ls[g]);
+          if (lane == 0) store_lse(a, hd.b, h0 + g, mx[g], ls[g]);
+        }
+        continue;
+      }
+      float *po = a.part_o + static_cast<int64_t>(hd.slot) * G * kHeadDim;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) __stcg(po + g * kHeadDim + lane + 32 * kk, acc[g][kk]);
+        if (lane == 0) __stcg(a.part_ml + static_cast<int64_t>(hd.slot) * G + g, make_float2(mx[g], ls[g]));
+      }
+      __syncwarp();  // the warp's partial stores precede lane 0's release
+      int ticket = 0;
+      if (lane == 0) {
+        __threadfence();
+        ticket = atomicAdd(a.counters + hd.pair, 1);
+      }
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket == hd.nsplit - 1) {  // last piece of the pair: merge all partials
+        __threadfence();
+        int pj, w;
+        pair_units(a, pl, hd.pair, &pj, &w);
+        combine_online_warp<G>(a, hd.b, hd.kvh, pair_slots(P, hd.pair, pj, w), lane);
+        if (lane == 0) atomicExch(a.counters + hd.pair, 0);
       }
     }
     return;
@@ -195,202 +327,146 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int hc = (lane & 3) * 2;     // heads of this lane's accumulator columns
   const int tr = t0 + (lane >> 2);   // token of this lane's S^T rows (and +8)
   const float sc = a.scale_log2;
-  // Completion ticket of the previous split piece, checked one piece later so
-  // the atomic's round trip overlaps the next piece's pages (thread 0 only).
-  bool pend = false;
-  int pend_ticket = 0, pend_b = 0, pend_kvh = 0, pend_nsplit = 0, pend_first = 0;
-  int *s_flag = pl.scratch + 8;  // [0] combine? [1] b [2] kvh [3] nsplit [4] first slot [5] more
 
-  int stage = 0;
-  uint32_t phase = 0;
-  for (int u = u_begin;;) {
-    const bool live = u < u_end;
-    Seg it;
-    if (live) {
-      it = locate_seg(a, pl, u, u_end, c, per);
-      u = it.u_next;
-      const int h0 = it.kvh * G;
-      uint32_t qb[8][2];
-      float o[8][4];
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-      float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
-
-      for (int p = it.p; p < it.p_end; ++p) {
-        const int valid = min(kPageTokens, it.ctx - p * kPageTokens);
-        mbar_wait_bounded(&full[stage], phase, a.error_flag);
-        const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
-        const uint32_t vbase = kbase + kPageBytes;
-        if (p == it.p) {  // q of this piece, staged with its first page
-          const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes + hc * 2;
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            uint32_t x0 = 0u, x1 = 0u;
-            if (qh < G) {
-              asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x0) : "r"(qs + ks * 32));
-              asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x1) : "r"(qs + ks * 32 + 16));
-            }
-            qb[ks][0] = x0;
-            qb[ks][1] = x1;
-          }
-        }
-        const bool partial = valid < t0 + 16;
-        if (partial) {  // zero this warp's V rows past the context (0 * NaN = NaN in the MMA)
-          for (int idx = lane; idx < 16 * 16; idx += 32) {
-            const int t = t0 + (idx >> 4), c = idx & 15;
-            if (t >= valid) st_shared_zero16(vbase + swz_off(c >> 3, t, c & 7));
-          }
-          __syncwarp();
-        }
-        // S^T = K . Q^T over the 128 dims (two independent accumulation chains)
-        float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int ks = 0; ks < 8; ks += 2) {
-          uint32_t ka[4], kb[4];
-          const int d = ks * 16 + k_dof;
-          ldsm_x4(kbase + swz_off(d >> 6, k_row, (d & 63) >> 3), ka);
-          ldsm_x4(kbase + swz_off((d + 16) >> 6, k_row, ((d + 16) & 63) >> 3), kb);
-          mma16816(s, ka, qb[ks][0], qb[ks][1]);
-          mma16816(s2, kb, qb[ks + 1][0], qb[ks + 1][1]);
-        }
-        // online softmax over this warp's 16 tokens, heads hc and hc + 1
-        const float x0 = tr < valid ? (s[0] + s2[0]) * sc : -CUDART_INF_F;
-        const float x1 = tr < valid ? (s[1] + s2[1]) * sc : -CUDART_INF_F;
-        const float x2 = tr + 8 < valid ? (s[2] + s2[2]) * sc : -CUDART_INF_F;
-        const float x3 = tr + 8 < valid ? (s[3] + s2[3]) * sc : -CUDART_INF_F;
-        const float mn0 = fmaxf(m0, quad_max(fmaxf(x0, x2)));
-        const float mn1 = fmaxf(m1, quad_max(fmaxf(x1, x3)));
-        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f, al0 = 1.f, al1 = 1.f;
-        if (mn0 != -CUDART_INF_F) {
-          p0 = exp2f(x0 - mn0);
-          p2 = exp2f(x2 - mn0);
-          al0 = exp2f(m0 - mn0);
-        }
-        if (mn1 != -CUDART_INF_F) {
-          p1 = exp2f(x1 - mn1);
-          p3 = exp2f(x3 - mn1);
-          al1 = exp2f(m1 - mn1);
-        }
-        l0 = l0 * al0 + quad_sum(p0 + p2);
-        l1 = l1 * al1 + quad_sum(p1 + p3);
-        m0 = mn0;
-        m1 = mn1;
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          o[mt][0] *= al0;
-          o[mt][1] *= al1;
-          o[mt][2] *= al0;
-          o[mt][3] *= al1;
-        }
-        const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the warp
-        const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
-        // O^T += V^T . P^T, 8 tiles of 16 dims
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          const int d = mt * 16 + v_dof;
-          uint32_t va[4];
-          ldsm_x4_t(vbase + swz_off(d >> 6, v_row, (d & 63) >> 3), va);
-          mma16816(o[mt], va, pb0, pb1);
-        }
-        if (partial) fence_proxy_async_smem();  // zero stores before the next TMA write
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        if (++stage == NST) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-
-      // ---- merge the 4 warps' states -----------------------------------
+  // Hands this warp's state of the finished piece (or the end marker) to the
+  // epilogue through piece buffer k & 1.
+  auto hand_off = [&](int k, const StageDesc &d, bool end, const float (&o)[8][4], float m0,
+                      float m1, float l0, float l1) {
+    const int pb = k & 1;
+    mbar_wait_bounded(&pempty[pb], ((k >> 1) & 1) ^ 1u, a.error_flag);
+    uint8_t *buf = smem + L::kPiece + pb * kPieceBytes;
+    if (!end) {
+      float *wo = reinterpret_cast<float *>(buf + kPieceO);
+      float2 *wml = reinterpret_cast<float2 *>(buf + kPieceML);
       if (lane < 4) {
-        s_wml[warp * 8 + hc] = make_float2(m0, l0);
-        s_wml[warp * 8 + hc + 1] = make_float2(m1, l1);
+        wml[warp * 8 + hc] = make_float2(m0, l0);
+        wml[warp * 8 + hc + 1] = make_float2(m1, l1);
       }
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
-        const int d = mt * 16 + (lane >> 2);
-        float *w = s_wo + (warp * kHeadDim + d) * 8 + hc;
+        const int dd = mt * 16 + (lane >> 2);
+        float *w = wo + (warp * kHeadDim + dd) * 8 + hc;
         *reinterpret_cast<float2 *>(w) = make_float2(o[mt][0], o[mt][1]);
         *reinterpret_cast<float2 *>(w + 8 * 8) = make_float2(o[mt][2], o[mt][3]);
       }
-      consumer_sync();
-      const int d = tid;  // 128 consumer threads, one output dim each
-      float acc[G], mx[G], ls[G];
+    }
+    if (warp == 0 && lane == 0) {
+      PieceHeader *hd = reinterpret_cast<PieceHeader *>(buf + kPieceHdr);
+      hd->b = d.b;
+      hd->kvh = d.kvh;
+      hd->pair = d.pair;
+      hd->nsplit = d.nsplit;
+      hd->slot = d.slot;
+      hd->end = end;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&pfull[pb]);
+  };
+
+  uint32_t qb[8][2];
+  float o[8][4];
+  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+  int stage = 0, piece = 0;
+  uint32_t phase = 0;
+  for (;;) {
+    mbar_wait_bounded(&full[stage], phase, a.error_flag);
+    const StageDesc d = descs[stage];
+    if (d.flags & kDescEnd) {
+      hand_off(piece, d, true, o, m0, m1, l0, l1);
+      break;
+    }
+    const bool first = d.flags & kDescFirst, last = d.flags & kDescLast;
+    const bool has = d.flags & kDescPage;
+    const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
+    const uint32_t vbase = kbase + kPageBytes;
+    if (first) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float m = -CUDART_INF_F;
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      m0 = m1 = -CUDART_INF_F;
+      l0 = l1 = 0.f;
+      if (has) {  // q of this piece, staged with its first page
+        const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes + hc * 2;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, s_wml[w * 8 + g].x);
-        float l = 0.f, x = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          const float2 ml = s_wml[w * 8 + g];
-          const float sc_w = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - m);
-          l = fmaf(ml.y, sc_w, l);
-          x = fmaf(s_wo[(w * kHeadDim + d) * 8 + g], sc_w, x);
-        }
-        acc[g] = x;
-        mx[g] = m;
-        ls[g] = l;
-      }
-      if (it.nsplit == 1) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          store_out(a, it.b, h0 + g, d, acc[g], ls[g]);
-          if (d == 0) store_lse(a, it.b, h0 + g, mx[g], ls[g]);
-        }
-      } else {
-        float *po = a.part_o + static_cast<int64_t>(it.slot) * G * kHeadDim;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          __stcg(po + g * kHeadDim + d, acc[g]);
-          if (d == 0) __stcg(a.part_ml + static_cast<int64_t>(it.slot) * G + g, make_float2(mx[g], ls[g]));
+        for (int ks = 0; ks < 8; ++ks) {
+          uint32_t x0 = 0u, x1 = 0u;
+          if (qh < G) {
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x0) : "r"(qs + ks * 32));
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x1) : "r"(qs + ks * 32 + 16));
+          }
+          qb[ks][0] = x0;
+          qb[ks][1] = x1;
         }
       }
     }
-    // ---- completion tickets (split pieces) and deferred combine -----------
-    consumer_sync();  // partial stores of every consumer thread precede the ticket
-    if (tid == 0) {
-      s_flag[0] = 0;
-      if (pend) {
-        if (pend_ticket == pend_nsplit - 1) {
-          s_flag[0] = 1;
-          s_flag[1] = pend_b;
-          s_flag[2] = pend_kvh;
-          s_flag[3] = pend_nsplit;
-          s_flag[4] = pend_first;
+    if (has) {
+      const int valid = min(kPageTokens, d.ctx - d.page * kPageTokens);
+      const bool partial = valid < t0 + 16;
+      if (partial) {  // zero this warp's V rows past the context (0 * NaN = NaN in the MMA)
+        for (int idx = lane; idx < 16 * 16; idx += 32) {
+          const int t = t0 + (idx >> 4), cc = idx & 15;
+          if (t >= valid) st_shared_zero16(vbase + swz_off(cc >> 3, t, cc & 7));
         }
-        pend = false;
+        __syncwarp();
       }
-      if (live && it.nsplit > 1) {
-        // releases this CTA's partial (cumulative over the barrier above)
-        pend_ticket = atomic_add_acq_rel_gpu(a.counters + it.pair, 1);
-        pend = true;
-        pend_b = it.b;
-        pend_kvh = it.kvh;
-        pend_nsplit = it.nsplit;
-        pend_first = it.first_slot;
+      // S^T = K . Q^T over the 128 dims (two independent accumulation chains)
+      float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 8; ks += 2) {
+        uint32_t ka[4], kb[4];
+        const int dd = ks * 16 + k_dof;
+        ldsm_x4(kbase + swz_off(dd >> 6, k_row, (dd & 63) >> 3), ka);
+        ldsm_x4(kbase + swz_off((dd + 16) >> 6, k_row, ((dd + 16) & 63) >> 3), kb);
+        mma16816(s, ka, qb[ks][0], qb[ks][1]);
+        mma16816(s2, kb, qb[ks + 1][0], qb[ks + 1][1]);
       }
-      s_flag[5] = live || pend;  // one drain round settles the last ticket
+      // online softmax over this warp's 16 tokens, heads hc and hc + 1
+      const float x0 = tr < valid ? (s[0] + s2[0]) * sc : -CUDART_INF_F;
+      const float x1 = tr < valid ? (s[1] + s2[1]) * sc : -CUDART_INF_F;
+      const float x2 = tr + 8 < valid ? (s[2] + s2[2]) * sc : -CUDART_INF_F;
+      const float x3 = tr + 8 < valid ? (s[3] + s2[3]) * sc : -CUDART_INF_F;
+      const float mn0 = fmaxf(m0, quad_max(fmaxf(x0, x2)));
+      const float mn1 = fmaxf(m1, quad_max(fmaxf(x1, x3)));
+      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f, al0 = 1.f, al1 = 1.f;
+      if (mn0 != -CUDART_INF_F) {
+        p0 = exp2f(x0 - mn0);
+        p2 = exp2f(x2 - mn0);
+        al0 = exp2f(m0 - mn0);
+      }
+      if (mn1 != -CUDART_INF_F) {
+        p1 = exp2f(x1 - mn1);
+        p3 = exp2f(x3 - mn1);
+        al1 = exp2f(m1 - mn1);
+      }
+      l0 = l0 * al0 + quad_sum(p0 + p2);
+      l1 = l1 * al1 + quad_sum(p1 + p3);
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+      }
+      const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the warp
+      const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
+      // O^T += V^T . P^T, 8 tiles of 16 dims
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int dd = mt * 16 + v_dof;
+        uint32_t va[4];
+        ldsm_x4_t(vbase + swz_off(dd >> 6, v_row, (dd & 63) >> 3), va);
+        mma16816(o[mt], va, pb0, pb1);
+      }
+      if (partial) fence_proxy_async_smem();  // zero stores before the next TMA write
     }
-    consumer_sync();
-    if (s_flag[0]) {
-      Item cit;
-      cit.b = s_flag[1];
-      cit.kvh = s_flag[2];
-      cit.nsplit = s_flag[3];
-      cit.split = cit.p = cit.p_end = cit.ctx = 0;
-      __threadfence();  // acquire the other CTAs' partials
-      if (cit.nsplit <= 4)
-        combine_partials_regs<G, 4>(a, cit, s_flag[4], tid);
-      else
-        combine_partials_staged<G, kConsumerWarps * 32>(a, cit, s_flag[4], tid, s_wo,
-                                                        kConsumerWarps * kHeadDim * 8, consumer_sync);
-      if (tid == 0) atomicExch(a.counters + cit.b * a.hkv + cit.kvh, 0);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == NST) {
+      stage = 0;
+      phase ^= 1u;
     }
-    const bool more = s_flag[5] != 0;
-    consumer_sync();  // s_wo / s_wml / flags are reused by the next round
-    if (!more) break;
+    if (last) hand_off(piece++, d, false, o, m0, m1, l0, l1);
   }
 }
 
@@ -408,11 +484,20 @@ int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int 
     B200KV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
     __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
   }
-  // one partition (CTA) per SM by default; `partitions` overrides the count
+  // one CTA per SM by default; `partitions` (<= kMaxPartitions) overrides it
   const int grid = partitions > 0 ? partitions : sms;
   a.target_items = grid;
-  kern<<<grid, kMmaThreads, L::kAlloc, stream>>>(km, vm, a);
-  B200KV_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMmaThreads);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200KV_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, km, vm, a));
   return B200KV_OK;
 }
 

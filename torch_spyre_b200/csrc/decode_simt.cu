@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
       if (pl.scratch[0]) {
         __threadfence();
-        combine_partials<G, kThreads>(a, it, item - it.split, tid);
+        combine_partials<G, kThreads>(a, it, SlotMap{item - it.split, it.nsplit}, tid);
         if (tid == 0) atomicExch(a.counters + it.b * a.hkv + it.kvh, 0);
       }
     }
