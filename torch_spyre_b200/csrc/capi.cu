@@ -63,6 +63,11 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
+#ifndef B200KV_L2_PROMOTION
+#define B200KV_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
+constexpr CUtensorMapL2promotion kPagePromotion = B200KV_L2_PROMOTION;
+
 int make_page_pool_map(CUtensorMap *map, const void *pool, int64_t num_blocks,
                        int64_t num_kv_heads) {
   EncodeTiledFn enc = encode_tiled_fn();
@@ -83,7 +88,7 @@ int make_page_pool_map(CUtensorMap *map, const void *pool, int64_t num_blocks,
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(pool), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_SWIZZLE_128B, kPagePromotion,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(B200KV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));

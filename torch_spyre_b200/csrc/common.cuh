@@ -111,9 +111,13 @@ __device__ __forceinline__ void mbar_wait_bounded(uint64_t *bar, uint32_t parity
   if (error_flag) atomicOr(error_flag, B200KV_DEVERR_TIMEOUT);
 }
 
+// L2 policy of the streamed KV pages (read once per launch): evict first.
+#ifndef B200KV_KV_POLICY
+#define B200KV_KV_POLICY "evict_first"
+#endif
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile("createpolicy.fractional.L2::" B200KV_KV_POLICY ".b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
 
