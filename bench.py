@@ -400,10 +400,11 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
             "q": s.q.cpu(),
             "k_new": torch.randn((B, hkv, D), dtype=torch.float16),
             "v_new": torch.randn((B, hkv, D), dtype=torch.float16),
-            "slots": slots,
             "block_table": bt_cpu,
             "context_lens": s.context_lens.cpu(),
         }
+        if tp:  # the TP step appends with kv_append, which takes explicit slots
+            parts["slots"] = slots
         offs, total = {}, 0
         for k, t in parts.items():
             offs[k] = total
@@ -431,15 +432,16 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
         s = sets[i]
         host, dev, v, h_out, _ = staged[i]
         dev.copy_(host, non_blocking=True)
-        tsb.kv_append(v["k_new"], v["v_new"], s.k_pool, s.v_pool, v["slots"])
         if tp:
             from torch_spyre_b200.tp import HeadShard, tp_decode_step
 
+            tsb.kv_append(v["k_new"], v["v_new"], s.k_pool, s.v_pool, v["slots"])
             shard = HeadShard(int(os.environ.get("RANK", "0")), world, cfg.num_q_heads, cfg.num_kv_heads,
                               cfg.head_dim)
             o = tp_decode_step(shard, v["q"], s.k_pool, s.v_pool, v["block_table"], v["context_lens"], w_o)
-        else:
-            o = tsb.decode_attention(v["q"], s.k_pool, s.v_pool, v["block_table"], v["context_lens"])
+        else:  # one launch: append the new token's K/V rows and decode
+            o = tsb.decode_attention_append(v["q"], v["k_new"], v["v_new"], s.k_pool, s.v_pool,
+                                            v["block_table"], v["context_lens"])
         h_out.copy_(o, non_blocking=True)
 
     def eager_round():
@@ -476,7 +478,8 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
     tokens = B if tp else B * world
     return {"value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms, 5),
-            "path": ("torch.ops.b200kv.kv_append + decode_attention with pinned host buffers, "
+            "path": ("torch.ops.b200kv.decode_attention_append (tp70b: kv_append + decode_attention + o_proj"
+                     " + all-reduce) with pinned host buffers, "
                      + ("captured once in a CUDA graph and replayed per step" if graph_ms is not None
                         else "eager")),
             "eager": {"value": round(tokens / (eager_ms / 1e3), 1), "ms_per_step": round(eager_ms, 5)}}

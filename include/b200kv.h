@@ -140,6 +140,28 @@ B200KV_API int b200kv_decode_attention_f16(
     void *workspace, int64_t workspace_bytes, int32_t *error_flag,
     void *stream);
 
+/* Decode attention fused with the KV append of the token being decoded (one
+ * launch instead of an append kernel followed by decode).  Each sequence's
+ * context length includes the new token, at position context_lens[b] - 1;
+ * its K/V rows k_new/v_new[b * new_stride_b + h * new_stride_h + d] are written
+ * into that position of the pools (page block_table[b][(len - 1) / 64]) and
+ * used for the attention of this step.  Replaces the reference's two-step HF
+ * path: cache.index_copy_ (torch_spyre/ops/fallbacks.py:256; test pattern
+ * tests/inductor/test_inductor_ops.py:5715-5740) followed by SDPA
+ * (torch_spyre/_inductor/decompositions.py:523-611).  Other arguments as in
+ * b200kv_decode_attention_f16; the pools are written.  A block id out of range
+ * skips the write (B200KV_DEVERR_BAD_BLOCK). */
+B200KV_API int b200kv_decode_attention_append_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new,
+    const void *v_new, int64_t new_stride_b, int64_t new_stride_h, void *k_pool,
+    void *v_pool, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference:
  * it exists for callers that cannot call cudaMalloc or any allocator when they
  * launch decode (an engine replaying pre-planned memory, a plugin host that

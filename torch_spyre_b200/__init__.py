@@ -8,12 +8,14 @@ is loaded on first use and is the only implementation.
 from . import _lib, layout, ops, workloads  # noqa: F401
 from ._lib import B200KVError
 from .layout import SpyreTensorLayout, empty_pool, page_layout, pool_shape, stick_layout
-from .ops import decode_attention, kv_append, kv_relayout, kv_unrelayout, sdpa_decode
+from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout,
+                  sdpa_decode)
 
 __all__ = [
     "B200KVError",
     "SpyreTensorLayout",
     "decode_attention",
+    "decode_attention_append",
     "empty_pool",
     "kv_append",
     "kv_relayout",

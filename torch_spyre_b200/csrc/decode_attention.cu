@@ -45,13 +45,14 @@ extern "C" int64_t b200kv_decode_workspace_bytes(int64_t batch, int64_t num_q_he
   return workspace_layout(batch, num_q_heads, num_kv_heads).total;
 }
 
-extern "C" int b200kv_decode_attention_f16(
+static int decode_entry(
     const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool, const void *v_pool,
     const int32_t *block_table, int64_t block_table_stride, const int32_t *context_lens, void *out,
     int64_t out_stride_b, int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
     int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq,
     float scale, int64_t num_splits, void *workspace, int64_t workspace_bytes,
-    int32_t *error_flag, void *stream) {
+    int32_t *error_flag, void *stream, const void *k_new, const void *v_new, int64_t new_sb,
+    int64_t new_sh, bool append) {
   clear_error();
   B200KV_CHECK_ARG(batch >= 0, "batch must be >= 0");
   B200KV_CHECK_ARG(num_q_heads > 0 && num_kv_heads > 0, "head counts must be > 0");
@@ -91,6 +92,15 @@ extern "C" int b200kv_decode_attention_f16(
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return set_error(B200KV_ERR_WORKSPACE, "workspace must be 256-byte aligned");
 
+  if (append) {
+    B200KV_CHECK_ARG(k_new && v_new, "k_new / v_new must not be null");
+    B200KV_CHECK_ARG((reinterpret_cast<uintptr_t>(k_new) & 15u) == 0 &&
+                         (reinterpret_cast<uintptr_t>(v_new) & 15u) == 0 && new_sb % 8 == 0 &&
+                         new_sh % 8 == 0,
+                     "new K/V rows must be 16-byte aligned with strides that are multiples of 8");
+    if (use_simt_kernel())
+      return set_error(B200KV_ERR_UNSUPPORTED, "fused append needs the tensor-core kernel");
+  }
   CUtensorMap km, vm;
   int st = make_page_pool_map(&km, k_pool, num_blocks, num_kv_heads);
   if (st != B200KV_OK) return st;
@@ -120,6 +130,14 @@ extern "C" int b200kv_decode_attention_f16(
   a.part_ml = reinterpret_cast<float2 *>(ws + wl.ml_off);
   a.part_o = reinterpret_cast<float *>(ws + wl.o_off);
   a.error_flag = error_flag;
+  if (append) {
+    a.k_new = static_cast<const __half *>(k_new);
+    a.v_new = static_cast<const __half *>(v_new);
+    a.new_sb = new_sb;
+    a.new_sh = new_sh;
+    a.k_pool_w = static_cast<__half *>(const_cast<void *>(k_pool));
+    a.v_pool_w = static_cast<__half *>(const_cast<void *>(v_pool));
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_simt_kernel()) {
     // CUDA-core variant: num_splits is its target number of work items per CTA
@@ -129,4 +147,32 @@ extern "C" int b200kv_decode_attention_f16(
   }
   // tensor-core kernel: num_splits is the number of equal KV partitions (CTAs)
   return launch_decode_mma(static_cast<int>(group), km, vm, a, static_cast<int>(num_splits), s);
+}
+
+extern "C" int b200kv_decode_attention_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool, const void *v_pool,
+    const int32_t *block_table, int64_t block_table_stride, const int32_t *context_lens, void *out,
+    int64_t out_stride_b, int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq,
+    float scale, int64_t num_splits, void *workspace, int64_t workspace_bytes,
+    int32_t *error_flag, void *stream) {
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, nullptr, nullptr, 0, 0, false);
+}
+
+extern "C" int b200kv_decode_attention_append_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new, const void *v_new,
+    int64_t new_stride_b, int64_t new_stride_h, void *k_pool, void *v_pool,
+    const int32_t *block_table, int64_t block_table_stride, const int32_t *context_lens, void *out,
+    int64_t out_stride_b, int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq,
+    float scale, int64_t num_splits, void *workspace, int64_t workspace_bytes,
+    int32_t *error_flag, void *stream) {
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
+                      new_stride_h, true);
 }

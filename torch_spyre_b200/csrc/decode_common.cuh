@@ -36,6 +36,11 @@ struct DecodeArgs {
   float2 *part_ml;   // [slots][G] (max in log2 units, sum of exp2)
   float *part_o;     // [slots][G][128] unnormalised partial outputs
   int32_t *error_flag;
+  // Fused append (null when not appending): the rows of the token at position
+  // context_len - 1 of each sequence, written into the pools and used for it.
+  const __half *k_new = nullptr, *v_new = nullptr;
+  int64_t new_sb = 0, new_sh = 0;
+  __half *k_pool_w = nullptr, *v_pool_w = nullptr;
 };
 
 struct WorkspaceLayout {
@@ -321,6 +326,11 @@ __device__ __forceinline__ Piece locate_piece(const DecodeArgs &a, const Plan &p
   s.slot = s.pair + c;
   s.u_next = hi_u;
   return s;
+}
+
+// Block id of page p of sequence b as stored (may be out of range).
+__device__ __forceinline__ int page_block_raw(const DecodeArgs &a, int b, int p) {
+  return __ldg(a.block_table + static_cast<int64_t>(b) * a.bt_stride + p);
 }
 
 // Block id of page p of sequence b, clamped into the pool (bad ids are

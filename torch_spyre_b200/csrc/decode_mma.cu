@@ -64,8 +64,9 @@ struct MmaSmem {
   static constexpr int kStageBytes = 2 * kPageBytes;                     // K page + V page
   static constexpr int kQ = NST * kStageBytes;                           // q slot per stage
   static constexpr int kPiece = kQ + NST * kQSlotBytes;                  // piece buffers
-  static constexpr int kDesc = kPiece + kPieceBufs * kPieceBytes;        // StageDesc [NST]
-  static constexpr int kPlan = kDesc + NST * 32;
+  static constexpr int kNew = kPiece + kPieceBufs * kPieceBytes;         // new K+V row per stage
+  static constexpr int kDesc = kNew + NST * 2 * kHeadDim * 2;            // StageDesc [NST]
+  static constexpr int kPlan = kDesc + NST * 48;
   static constexpr int kBars = (kPlan + kPlanBytes + 7) & ~7;  // full, empty [NST]; pfull, pempty [2]
   static constexpr int kBytes = kBars + (2 * NST + 2 * kPieceBufs) * 8;
   static constexpr int kAlloc = kBytes + 1024;
@@ -74,12 +75,13 @@ struct MmaSmem {
 // What one stage carries, written by the producer before it arms the stage's
 // full barrier: the piece (pair, slot, split count), the page and flags.
 struct StageDesc {
-  int b, kvh, pair, page, ctx, nsplit, slot, flags;
+  int b, kvh, pair, page, ctx, nsplit, slot, flags, blk, pad[3];
 };
 constexpr int kDescFirst = 1;  // first page of a piece
 constexpr int kDescLast = 2;   // last page of a piece
 constexpr int kDescPage = 4;   // the stage holds a page (an empty sequence has none)
 constexpr int kDescEnd = 8;    // no more work for this CTA
+constexpr int kDescNew = 16;   // the stage carries the appended token's K/V rows
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -128,7 +130,7 @@ __device__ __forceinline__ float quad_sum(float v) {
   return v + __shfl_xor_sync(0xffffffffu, v, 16);
 }
 
-template <int G, int NST>
+template <int G, int NST, bool kAppend>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
@@ -188,9 +190,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         const int nstages = max(npages, 1);  // an empty sequence still takes one stage
         for (int base = 0; base < nstages; base += 32) {
           const int n = min(32, nstages - base);
-          const int my_blk = (lane < n && npages > 0) ? page_block(a, pc.b, pc.p + base + lane) : 0;
+          const int my_raw = (lane < n && npages > 0) ? page_block_raw(a, pc.b, pc.p + base + lane) : 0;
+          const int my_blk = (my_raw < 0 || my_raw >= a.num_blocks) ? page_block(a, pc.b, pc.p + base + lane) : my_raw;
           for (int j = 0; j < n; ++j) {
             const int blk = __shfl_sync(0xffffffffu, my_blk, j);
+            const int raw = kAppend ? __shfl_sync(0xffffffffu, my_raw, j) : 0;
             if (lane == 0) {
               mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
               const int i = base + j;
@@ -203,11 +207,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               d.ctx = pc.ctx;
               d.nsplit = pc.nsplit;
               d.slot = pc.slot;
+              // the appended token (position ctx - 1) lies on this page
+              const bool app = kAppend && has && (pc.ctx - 1) / kPageTokens == pc.p + i;
+              if (kAppend) d.blk = (raw >= 0 && raw < a.num_blocks) ? raw : -1;
               d.flags = (i == 0 ? kDescFirst : 0) | (i == nstages - 1 ? kDescLast : 0) |
-                        (has ? kDescPage : 0);
+                        (has ? kDescPage : 0) | (app ? kDescNew : 0);
               uint32_t tx = has ? 2 * kPageBytes : 0;
               if (has && i == 0) tx += G * kHeadDim * 2;
+              if (app) tx += 2 * kHeadDim * 2;
               mbar_arrive_expect_tx(&full[stage], tx);
+              if (kAppend && app) {
+                uint8_t *ns = smem + L::kNew + stage * 2 * kHeadDim * 2;
+                const int64_t off = pc.b * a.new_sb + pc.kvh * a.new_sh;
+                bulk_load(ns, a.k_new + off, kHeadDim * 2, &full[stage]);
+                bulk_load(ns + kHeadDim * 2, a.v_new + off, kHeadDim * 2, &full[stage]);
+              }
               if (has) {
                 if (i == 0) {  // the piece's q rows ride on its first page's barrier
                   uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
@@ -398,6 +412,27 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         }
       }
     }
+    bool wrote_smem = false;
+    if (kAppend && (d.flags & kDescNew)) {  // appended token: its rows replace the staged ones
+      const int t_new = (d.ctx - 1) % kPageTokens;
+      if ((t_new >> 4) == warp) {
+        const int c = lane & 15;  // 16-byte chunk of the row; lanes 0-15 K, 16-31 V
+        const int kv = lane >> 4;
+        const uint8_t *src = smem + L::kNew + stage * 2 * kHeadDim * 2 + kv * kHeadDim * 2 + c * 16;
+        const uint4 v = *reinterpret_cast<const uint4 *>(src);
+        *reinterpret_cast<uint4 *>(smem + stage * L::kStageBytes + kv * kPageBytes +
+                                   swz_off(c >> 3, t_new, c & 7)) = v;
+        if (d.blk >= 0) {
+          __half *pool = kv ? a.v_pool_w : a.k_pool_w;
+          const int64_t off = ((static_cast<int64_t>(d.blk) * a.hkv + d.kvh) * kSticks + (c >> 3)) *
+                                  (kPageTokens * kStickElems) +
+                              t_new * kStickElems + (c & 7) * 8;
+          *reinterpret_cast<uint4 *>(pool + off) = v;
+        }
+        wrote_smem = true;
+      }
+      __syncwarp();
+    }
     if (has) {
       const int valid = min(kPageTokens, d.ctx - d.page * kPageTokens);
       const bool partial = valid < t0 + 16;
@@ -458,7 +493,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         ldsm_x4_t(vbase + swz_off(dd >> 6, v_row, (dd & 63) >> 3), va);
         mma16816(o[mt], va, pb0, pb1);
       }
-      if (partial) fence_proxy_async_smem();  // zero stores before the next TMA write
+      if (partial || wrote_smem) fence_proxy_async_smem();  // st.shared before the next TMA write
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
@@ -470,12 +505,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
 }
 
-template <int G, int NST>
-int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
-               cudaStream_t stream) {
+template <int G, int NST, bool kAppend>
+int launch_mma_impl(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
+                    cudaStream_t stream) {
   using L = MmaSmem<NST>;
   static_assert(L::kAlloc <= 227 * 1024, "shared memory budget");
-  auto kern = decode_mma_kernel<G, NST>;
+  auto kern = decode_mma_kernel<G, NST, kAppend>;
   int dev = 0, sms = 0;
   int st = current_device_sm_count(&dev, &sms);
   if (st != B200KV_OK) return st;
@@ -499,6 +534,13 @@ int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int 
   cfg.numAttrs = 1;
   B200KV_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, km, vm, a));
   return B200KV_OK;
+}
+
+template <int G, int NST>
+int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
+               cudaStream_t stream) {
+  if (a.k_new != nullptr) return launch_mma_impl<G, NST, true>(km, vm, a, partitions, stream);
+  return launch_mma_impl<G, NST, false>(km, vm, a, partitions, stream);
 }
 
 #ifndef B200KV_MMA_STAGES

@@ -9,6 +9,9 @@ Operator surface, mirroring the reference's hot-path ops:
   (torch_spyre/csrc/attn_utils.cpp:22-37 -> torch_spyre/_inductor/
   decompositions.py:523-611).  :func:`sdpa_decode` is the drop-in adapter with
   the SDPA signature and the reference's output memory order (596-600).
+* ``b200kv::decode_attention_append(q, k_new, v_new, k_pool!, v_pool!, ...)``
+  -- the same decode fused with the append of the new token (the HF
+  ``index_copy_`` + SDPA decode step, fallbacks.py:256 + decompositions.py).
 * ``b200kv::kv_append(k_new, v_new, k_pool!, v_pool!, slot_mapping)`` -- the
   KV slot write, in place like ``spyre::overwrite`` (customops.py:262-295,
   ``mutates_args``) and ``Tensor.index_copy_`` (ops/fallbacks.py:256).
@@ -170,6 +173,93 @@ def decode_attention(
         scale = 1.0 / math.sqrt(q.shape[-1])
     out, lse = torch.ops.b200kv.decode_attention(
         q, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
+    )
+    return (out, lse) if return_lse else out
+
+
+# ------------------------------------------------- fused append + decode --
+@torch.library.custom_op("b200kv::decode_attention_append", mutates_args=("k_pool", "v_pool"),
+                         device_types="cuda")
+def _decode_attention_append_op(
+    q: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_table: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: float,
+    num_splits: int,
+    error_flag: Optional[torch.Tensor],
+) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda(q, k_new, v_new, k_pool, v_pool, block_table, context_lens)
+    if q.dim() != 3 or q.dtype != torch.float16 or q.stride(2) != 1:
+        raise ValueError(f"q must be fp16 [B, Hq, D] with a contiguous head_dim, got {tuple(q.shape)}")
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    B, Hq, D = q.shape
+    NB, Hkv = k_pool.shape[0], k_pool.shape[1]
+    if k_new.shape != (B, Hkv, D) or v_new.shape != k_new.shape or k_new.dtype != torch.float16 \
+            or v_new.dtype != torch.float16 or k_new.stride() != v_new.stride() or k_new.stride(2) != 1:
+        raise ValueError("k_new / v_new must be fp16 [B, Hkv, D] with equal strides and a contiguous head_dim")
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.stride(1) != 1:
+        raise ValueError("block_table must be int32 [B, max_blocks] with unit column stride")
+    if context_lens.dtype != torch.int32 or context_lens.dim() != 1 or not context_lens.is_contiguous():
+        raise ValueError("context_lens must be a contiguous int32 [B] tensor")
+    out = torch.empty((B, Hq, D), dtype=torch.float16, device=q.device)
+    lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    if B == 0:
+        return out, lse
+    lib = _lib.lib()
+    wbytes = lib.b200kv_decode_workspace_bytes(B, Hq, Hkv, D)
+    ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
+    _lib.call(
+        "b200kv_decode_attention_append_f16",
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+        k_pool.data_ptr(), v_pool.data_ptr(),
+        block_table.data_ptr(), block_table.stride(0),
+        context_lens.data_ptr(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        lse.data_ptr(),
+        B, Hq, Hkv, D, NB, block_table.shape[1],
+        float(scale), int(num_splits),
+        ws.data_ptr(), ws.numel(),
+        _ptr(error_flag), _stream_ptr(q.device),
+    )
+    _maybe_check_flag(error_flag, "decode_attention_append")
+    return out, lse
+
+
+@_decode_attention_append_op.register_fake
+def _(q, k_new, v_new, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag):
+    B, Hq, D = q.shape
+    return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)
+
+
+def decode_attention_append(
+    q: torch.Tensor,
+    k_new: torch.Tensor,
+    v_new: torch.Tensor,
+    k_pool: torch.Tensor,
+    v_pool: torch.Tensor,
+    block_table: torch.Tensor,
+    context_lens: torch.Tensor,
+    scale: Optional[float] = None,
+    num_splits: int = 0,
+    return_lse: bool = False,
+    error_flag: Optional[torch.Tensor] = None,
+):
+    """Appends the new token's K/V rows ([B, Hkv, D], at position
+    context_lens[b] - 1) to the pools and decodes, in one launch.
+
+    Same result as ``kv_append`` at those slots followed by
+    ``decode_attention`` (the HF ``index_copy_`` + SDPA step of the reference).
+    """
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    out, lse = torch.ops.b200kv.decode_attention_append(
+        q, k_new, v_new, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
     )
     return (out, lse) if return_lse else out
 
