@@ -87,6 +87,27 @@ B200KV_API int b200kv_stick_layout(const int64_t *host_size, const int64_t *host
                         int64_t *device_size, int64_t *stride_map, int32_t cap,
                         int32_t *out_rank);
 
+/* General stick relayout between a strided tensor in host dim order and a
+ * device buffer laid out by (device_size, stride_map) -- the device-side form
+ * of the reference's `x.to(device_layout=stl)` / `.cpu()` copies, whose
+ * element map its DMA descriptors encode (generate_dci /
+ * get_device_stride_infos, torch_spyre/csrc/spyre_mem.cpp:176-440; dim
+ * matching get_dim_map 60-96; pinned by tests/tensor/test_tensor_layout.py:
+ * 152-280).  Both buffers are device memory.
+ *   direction 0: src = host-order tensor (sizes host_size, element strides
+ *                host_stride), dst = device buffer of prod(device_size)
+ *                elements; stick padding is written as zero.
+ *   direction 1: src = device buffer, dst = host-order tensor; only elements
+ *                inside the host tensor are written.
+ * elem_bytes 1, 2 or 4; ranks <= 8.  A stride_map entry that is not a
+ * multiple of the host stride it matches (a folded layout) is
+ * B200KV_ERR_UNSUPPORTED. */
+B200KV_API int b200kv_stick_relayout(const void *src, void *dst, int32_t elem_bytes,
+                                     int32_t host_rank, const int64_t *host_size,
+                                     const int64_t *host_stride, int32_t device_rank,
+                                     const int64_t *device_size, const int64_t *stride_map,
+                                     int32_t direction, void *stream);
+
 /* Bytes a layout occupies on the device: 128 B per stick times the product of
  * the non-stick device dims (spyre_tensor_impl.cpp:287-293). */
 B200KV_API int64_t b200kv_device_size_in_bytes(const int64_t *device_size,

@@ -34,3 +34,9 @@ def test_cpu_tensors_rejected():
         tsb.decode_attention(q, pool, pool, bt, ctx)
     with pytest.raises(Exception, match="CUDA"):
         tsb.kv_append(q, q, pool, pool, torch.zeros(1, dtype=torch.int64))
+
+
+def test_stick_relayout_rejects_cpu_tensors():
+    x = torch.zeros(4, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        tsb.to_device_layout(x, tsb.SpyreTensorLayout([4, 64], torch.float16))

@@ -7,7 +7,8 @@ is loaded on first use and is the only implementation.
 
 from . import _lib, layout, ops, workloads  # noqa: F401
 from ._lib import B200KVError
-from .layout import SpyreTensorLayout, empty_pool, page_layout, pool_shape, stick_layout
+from .layout import (SpyreTensorLayout, empty_pool, from_device_layout, page_layout, pool_shape, stick_layout,
+                     to_device_layout)
 from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout,
                   sdpa_decode)
 
@@ -17,6 +18,8 @@ __all__ = [
     "decode_attention",
     "decode_attention_append",
     "empty_pool",
+    "from_device_layout",
+    "to_device_layout",
     "kv_append",
     "kv_relayout",
     "kv_unrelayout",

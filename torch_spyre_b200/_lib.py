@@ -54,6 +54,10 @@ SIGNATURES = {
         [_p, _p, _i32, _p, _i32, _i32, _p, _p, _i32, _p],
     ),
     "b200kv_device_size_in_bytes": (_i64, [_p, _i32]),
+    "b200kv_stick_relayout": (
+        ctypes.c_int,
+        [_p, _p, _i32, _i32, _p, _p, _i32, _p, _p, _i32, _p],
+    ),
     "b200kv_decode_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "b200kv_decode_attention_f16": (
         ctypes.c_int,

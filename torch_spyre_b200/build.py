@@ -26,6 +26,7 @@ SOURCES = [
     "decode_mma.cu",
     "decode_simt.cu",
     "decode_noalloc.cu",
+    "stick_relayout.cu",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

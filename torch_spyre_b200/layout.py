@@ -96,6 +96,12 @@ class SpyreTensorLayout:
                             "(device_size, stride_map, dtype)")
         self.device_dtype = dtype
 
+    def device_numel(self) -> int:
+        n = 1
+        for x in self.device_size:
+            n *= x
+        return n
+
     def device_size_in_bytes(self) -> int:
         arr = (ctypes.c_int64 * len(self.device_size))(*self.device_size)
         return int(_lib.lib().b200kv_device_size_in_bytes(ctypes.cast(arr, ctypes.c_void_p), len(arr)))
@@ -134,3 +140,43 @@ def slot_of(block_table: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
     """Slots (block * 64 + offset) of token `positions[b]` of each sequence b."""
     blk = block_table.gather(1, (positions // PAGE_TOKENS).long().unsqueeze(1)).squeeze(1).long()
     return blk * PAGE_TOKENS + (positions % PAGE_TOKENS).long()
+
+
+def _arr64(v):
+    a = (ctypes.c_int64 * len(v))(*v)
+    return a, ctypes.cast(a, ctypes.c_void_p)
+
+
+def _stick_relayout(src: torch.Tensor, dst: torch.Tensor, host: torch.Tensor, stl: "SpyreTensorLayout",
+                    direction: int) -> None:
+    if src.device.type != "cuda" or dst.device.type != "cuda":
+        raise RuntimeError("stick relayout runs on CUDA devices only (there is no CPU fallback)")
+    hs, hs_p = _arr64(list(host.shape) or [1])
+    st, st_p = _arr64(list(host.stride()) or [1])
+    ds, ds_p = _arr64(stl.device_size)
+    sm, sm_p = _arr64(stl.stride_map)
+    _lib.call("b200kv_stick_relayout", src.data_ptr(), dst.data_ptr(), host.element_size(),
+              max(host.dim(), 1), hs_p, st_p, len(stl.device_size), ds_p, sm_p, direction,
+              torch.cuda.current_stream(src.device).cuda_stream)
+
+
+def to_device_layout(x: torch.Tensor, stl: SpyreTensorLayout) -> torch.Tensor:
+    """Device buffer (flat, prod(device_size) elements) holding x in layout stl.
+
+    The CUDA form of the reference's ``x.to(device_layout=stl)``
+    (torch_spyre/_monkey_patch.py:73-156 -> generate_dci); x may be a strided
+    view.  Stick padding is zero.
+    """
+    buf = torch.empty(stl.device_numel(), dtype=x.dtype, device=x.device)
+    _stick_relayout(x, buf, x, stl, 0)
+    return buf
+
+
+def from_device_layout(buf: torch.Tensor, stl: SpyreTensorLayout, host_size, out: Optional[torch.Tensor] = None
+                       ) -> torch.Tensor:
+    """The host-order tensor read back from a device-layout buffer (``.cpu()``
+    of the reference, on the device)."""
+    if out is None:
+        out = torch.empty(tuple(host_size), dtype=buf.dtype, device=buf.device)
+    _stick_relayout(buf, out, out, stl, 1)
+    return out
