@@ -62,6 +62,8 @@ def parse_args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--cpu-baseline-seconds", type=float, default=10.0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kv-dtype", default="fp16", choices=["fp16", "fp8"],
+                   help="KV page element type: fp16 (the reference's) or e4m3 pages with per-pool fp16 scales")
     p.add_argument("--nccl-graph", action="store_true",
                    help="tp70b at N > 1: capture the step, NCCL all-reduce included, in a CUDA graph")
     return p.parse_args()
@@ -183,6 +185,11 @@ def cpu_oracle_rate(inp, budget_s: float, max_steps: int | None = None):
 
     torch.set_num_threads(os.cpu_count() or 1)
     cpu = {k: getattr(inp, k).cpu() for k in ("q", "k_pool", "v_pool", "block_table", "context_lens")}
+    if inp.k_scale is not None:  # fp8 pages: the CPU path runs on the dequantized cache
+        from oracle import fp8_quant as o8
+
+        cpu["k_pool"] = o8.fp16_pool_from_pool(cpu["k_pool"], inp.k_scale.cpu())
+        cpu["v_pool"] = o8.fp16_pool_from_pool(cpu["v_pool"], inp.v_scale.cpu())
     B = len(inp.ctx)
     done, t0, b = 0, time.perf_counter(), 0
     while True:
@@ -197,17 +204,20 @@ def cpu_oracle_rate(inp, budget_s: float, max_steps: int | None = None):
 
 
 # ----------------------------------------------------------------- ours -----
-def build_inputs(cfg, rank, world, n_sets, device, start=0):
-    from torch_spyre_b200.workloads import make_decode_inputs
+def build_inputs(cfg, rank, world, n_sets, device, start=0, kv_dtype="fp16"):
+    from torch_spyre_b200.workloads import make_decode_inputs, quantize_decode_inputs
 
     sets = []
     for i in range(start, start + n_sets):
         if cfg.name == "tp70b":
             hkv = cfg.num_kv_heads // world
-            sets.append(make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}", num_kv_heads=hkv,
-                                           ctx=None))
+            inp = make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}", num_kv_heads=hkv, ctx=None)
         else:
-            sets.append(make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}"))
+            inp = make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}")
+        if kv_dtype == "fp8":  # the same step over e4m3 pages (quantized on the device)
+            inp = quantize_decode_inputs(inp)
+            torch.cuda.synchronize(device)
+        sets.append(inp)
     return sets
 
 
@@ -224,10 +234,11 @@ def run_ours(args, rank, world, local):
         raise SystemExit(f"tp70b needs N dividing {cfg.num_kv_heads}")
 
     # how many rotating input sets keep each step's reads out of L2
-    probe = build_inputs(cfg, rank, world, 1, device)[0]
+    fp8 = args.kv_dtype == "fp8"
+    probe = build_inputs(cfg, rank, world, 1, device, kv_dtype=args.kv_dtype)[0]
     n_sets = max(1, math.ceil(3 * L2_BYTES / probe.kv_bytes)) if probe.kv_bytes < 3 * L2_BYTES else 1
     n_sets = min(n_sets, 32)
-    sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1)
+    sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1, kv_dtype=args.kv_dtype)
     step_bytes = statistics.mean(s.step_bytes for s in sets)
     kv_bytes = statistics.mean(s.kv_bytes for s in sets)
     B = len(sets[0].ctx)
@@ -248,11 +259,13 @@ def run_ours(args, rank, world, local):
     def step(s):
         if tp:
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
-                                  out=partial)
-        return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
+                                  out=partial, k_scale=s.k_scale, v_scale=s.v_scale)
+        return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
+                                    v_scale=s.v_scale)
 
     def decode_only(s):
-        return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens)
+        return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
+                                    v_scale=s.v_scale)
 
     stream = torch.cuda.Stream(device)
 
@@ -334,16 +347,17 @@ def run_ours(args, rank, world, local):
     value = tokens_per_step * steps / (total_ms / 1e3)
 
     peak, peak_kind = hbm_peak()
+    kernel = "decode_kernel_fp8" if fp8 else "decode_kernel"
     # achieved bandwidth of the decode kernel (the only launch of a replicated
     # step; timed on its own for tp70b)
     achieved = step_bytes / (launch_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "traffic": (round(ratio * step_bytes) if (ratio := profiled_traffic_ratio("decode_kernel", args.workload))
+                "traffic": (round(ratio * step_bytes) if (ratio := profiled_traffic_ratio(kernel, args.workload))
                             else None),
-                "traffic_source": (f"ncu dram__bytes_read+write / algorithmic = {ratio} (profiles/decode_kernel_"
+                "traffic_source": (f"ncu dram__bytes_read+write / algorithmic = {ratio} (profiles/{kernel}_"
                                    f"{args.workload}.md), times this run's bytes per launch") if ratio else None,
-                "kernel": "decode_kernel", "algorithmic_bytes_per_launch": int(step_bytes),
+                "kernel": kernel, "algorithmic_bytes_per_launch": int(step_bytes),
                 "mean_launch_ms": round(launch_ms, 5)}
 
     e2e = None
@@ -355,17 +369,19 @@ def run_ours(args, rank, world, local):
         rate, n, el = cpu_oracle_rate(sets[0], args.cpu_baseline_seconds)
         cpu = {"value": round(rate, 3), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                "sample": f"{n} whole sequences of the {args.workload} batch (round robin), {el:.1f} s, "
-                         "paged gather + torch CPU SDPA fp32"}
+                         "paged gather + torch CPU SDPA fp32"
+                         + (" over the dequantized (fp16) pools" if fp8 else "")}
 
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": "e4m3 KV pages, f16 q/out (fp32 accumulate)" if fp8 else "f16 (fp32 accumulate)",
         "data": "synthetic (seeded N(0,1) fp16 q/K/V, seeded contexts and block permutations)",
         "config": {"workload": args.workload, "description": cfg.description, "batch_per_rank": B,
                    "global_batch": tokens_per_step, "num_q_heads": cfg.num_q_heads,
                    "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
-                   "kv_heads_per_rank": sets[0].k_pool.shape[1],
+                   "kv_heads_per_rank": sets[0].k_pool.shape[1], "kv_dtype": args.kv_dtype,
                    "parallelism": (f"tp{world} (kv-head shards + NCCL all-reduce)" if tp else f"dp{world} (sequence shards)"),
                    "l2": f"{n_sets} rotating input sets, {kv_bytes / 1e6:.1f} MB KV read per step (L2 126 MB)",
                    "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")},
@@ -435,13 +451,16 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
         if tp:
             from torch_spyre_b200.tp import HeadShard, tp_decode_step
 
-            tsb.kv_append(v["k_new"], v["v_new"], s.k_pool, s.v_pool, v["slots"])
+            tsb.kv_append(v["k_new"], v["v_new"], s.k_pool, s.v_pool, v["slots"], k_scale=s.k_scale,
+                          v_scale=s.v_scale)
             shard = HeadShard(int(os.environ.get("RANK", "0")), world, cfg.num_q_heads, cfg.num_kv_heads,
                               cfg.head_dim)
-            o = tp_decode_step(shard, v["q"], s.k_pool, s.v_pool, v["block_table"], v["context_lens"], w_o)
+            o = tp_decode_step(shard, v["q"], s.k_pool, s.v_pool, v["block_table"], v["context_lens"], w_o,
+                               k_scale=s.k_scale, v_scale=s.v_scale)
         else:  # one launch: append the new token's K/V rows and decode
             o = tsb.decode_attention_append(v["q"], v["k_new"], v["v_new"], s.k_pool, s.v_pool,
-                                            v["block_table"], v["context_lens"])
+                                            v["block_table"], v["context_lens"], k_scale=s.k_scale,
+                                            v_scale=s.v_scale)
         h_out.copy_(o, non_blocking=True)
 
     def eager_round():

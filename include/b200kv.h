@@ -237,6 +237,79 @@ B200KV_API int b200kv_relayout_f16(void *rows, void *pool, const int32_t *block_
                         int64_t head_dim, int64_t num_blocks, int32_t direction,
                         int32_t *error_flag, void *stream);
 
+/* ------------------------------------------------------------------------ *
+ * FP8 (e4m3) KV pages.
+ *
+ * An fp8 pool uses the reference's stick tiling for 1-byte elements: a stick
+ * is 128 elements (128 bytes), so a page of 64 tokens x D holds D/128 sticks:
+ *     k_pool, v_pool : e4m3 [num_blocks, num_kv_heads, D/128, 64, 128]
+ * (device_size [D/128, 64, 128], stride_map [128, D, 1];
+ * torch_spyre/csrc/spyre_tensor_impl.cpp:46-175).  Element (t, d) of page
+ * (blk, h) is at byte ((blk * Hkv + h) * D/128 + d / 128) * 8192 +
+ * (t % 64) * 128 + d % 128.  Each pool carries one fp16 scale (a device
+ * scalar): the stored value q stands for fp16(q) * scale, the reference's
+ * dequantize_fp8_with_scale (torch_spyre/_inductor/customops.py:624-653,
+ * decompositions.py:846-858); values are written with its
+ * quantize_fp8_with_scale (customops.py:587-621, decompositions.py:897-904):
+ *     q = e4m3_rne(clamp(fp16(x * fp16(1 / scale)), -448, 448)).
+ * ------------------------------------------------------------------------ */
+
+/* Quantize fp16 x [rows, cols] (contiguous) to e4m3 out [rows, cols] with the
+ * fp16 scale of row r at scale[r * scale_stride] (scale_stride 0: one scale
+ * for the whole tensor).  Replaces spyre::quantize_fp8_with_scale.  Bit-exact
+ * with the reference's CPU decomposition. */
+B200KV_API int b200kv_quantize_fp8_f16(const void *x, void *out, int64_t rows,
+                                       int64_t cols, const void *scale,
+                                       int64_t scale_stride, void *stream);
+
+/* Dequantize e4m3 x [rows, cols] to fp16 out: fp16(x) * scale[r * scale_stride].
+ * Replaces spyre::dequantize_fp8_with_scale.  Bit-exact. */
+B200KV_API int b200kv_dequantize_fp8_f16(const void *x, void *out, int64_t rows,
+                                         int64_t cols, const void *scale,
+                                         int64_t scale_stride, void *stream);
+
+/* KV append into fp8 pools: as b200kv_kv_append_f16, with each fp16 row
+ * quantized with the pool's scale (k_scale / v_scale: device fp16 scalars). */
+B200KV_API int b200kv_kv_append_fp8(const void *k_new, const void *v_new,
+                                    int64_t new_stride_n, int64_t new_stride_h,
+                                    void *k_pool, void *v_pool,
+                                    const void *k_scale, const void *v_scale,
+                                    const int64_t *slot_mapping, int64_t num_tokens,
+                                    int64_t num_kv_heads, int64_t head_dim,
+                                    int64_t num_blocks, int32_t *error_flag,
+                                    void *stream);
+
+/* Decode attention over fp8 pools: as b200kv_decode_attention_f16 with
+ * K = fp16(k_pool) * k_scale and V = fp16(v_pool) * v_scale (device fp16
+ * scalars).  q, out, lse and the workspace are as in the fp16 call.  The
+ * scales are applied in fp32 (to the scores and to the output) instead of
+ * rounding each dequantized element to fp16. */
+B200KV_API int b200kv_decode_attention_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
+    const void *v_pool, const void *k_scale, const void *v_scale,
+    const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream);
+
+/* Fused append + decode over fp8 pools: as
+ * b200kv_decode_attention_append_f16, the new fp16 rows quantized into the
+ * pools (as b200kv_kv_append_fp8) and used, quantized, for this step. */
+B200KV_API int b200kv_decode_attention_append_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new,
+    const void *v_new, int64_t new_stride_b, int64_t new_stride_h, void *k_pool,
+    void *v_pool, const void *k_scale, const void *v_scale,
+    const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream);
+
 #ifdef __cplusplus
 }
 #endif

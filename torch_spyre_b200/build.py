@@ -27,6 +27,7 @@ SOURCES = [
     "decode_simt.cu",
     "decode_noalloc.cu",
     "stick_relayout.cu",
+    "fp8_ops.cu",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

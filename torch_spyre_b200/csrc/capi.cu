@@ -69,7 +69,7 @@ EncodeTiledFn encode_tiled_fn() {
 constexpr CUtensorMapL2promotion kPagePromotion = B200KV_L2_PROMOTION;
 
 int make_page_pool_map(CUtensorMap *map, const void *pool, int64_t num_blocks,
-                       int64_t num_kv_heads) {
+                       int64_t num_kv_heads, int elem_bytes) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return set_error(B200KV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   if ((reinterpret_cast<uintptr_t>(pool) & 15u) != 0)
@@ -78,15 +78,19 @@ int make_page_pool_map(CUtensorMap *map, const void *pool, int64_t num_blocks,
   if (pages <= 0 || pages > (int64_t{1} << 31) - 1)
     return set_error(B200KV_ERR_INVALID_ARG, "pool page count %lld out of range",
                      static_cast<long long>(pages));
-  // dim0: 64 elements of a stick (128 B), dim1: S*64 stick rows of a page,
+  if (elem_bytes != 1 && elem_bytes != 2)
+    return set_error(B200KV_ERR_INVALID_ARG, "page element size %d", elem_bytes);
+  // dim0: the elements of one 128-byte stick, dim1: S*64 stick rows of a page,
   // dim2: pages (block * Hkv + head).
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kStickElems),
-                        static_cast<cuuint64_t>(kSticks * kPageTokens),
-                        static_cast<cuuint64_t>(pages)};
-  cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(kPageBytes)};
-  cuuint32_t box[3] = {kStickElems, kSticks * kPageTokens, 1};
+  const bool fp8 = elem_bytes == 1;
+  const cuuint32_t stick = fp8 ? kStickElemsFp8 : kStickElems;
+  const cuuint32_t rows = (fp8 ? kSticksFp8 : kSticks) * kPageTokens;
+  cuuint64_t dims[3] = {stick, rows, static_cast<cuuint64_t>(pages)};
+  cuuint64_t strides[2] = {128, static_cast<cuuint64_t>(fp8 ? kPageBytesFp8 : kPageBytes)};
+  cuuint32_t box[3] = {stick, rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(pool), dims,
+  CUresult r = enc(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   const_cast<void *>(pool), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, kPagePromotion,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

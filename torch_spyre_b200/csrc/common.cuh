@@ -22,6 +22,11 @@ constexpr int kSticks = kHeadDim / kStickElems;               // 2
 constexpr int kPageElems = kPageTokens * kHeadDim;            // 8192
 constexpr int kPageBytes = kPageElems * 2;                    // 16 KiB
 constexpr int kStickBytes = kPageTokens * kStickElems * 2;    // 8 KiB per stick column
+// fp8 (e4m3) pages: a 128-byte stick holds 128 elements, so a D = 128 page is
+// one stick column of 64 token rows.
+constexpr int kStickElemsFp8 = 128;
+constexpr int kSticksFp8 = kHeadDim / kStickElemsFp8;         // 1
+constexpr int kPageBytesFp8 = kPageTokens * kHeadDim;         // 8 KiB
 
 // ---------------------------------------------------------------- status ----
 // Sets the calling thread's last-error message and returns `code`.
@@ -52,10 +57,12 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled_fn();
 
-// Tensor map over a page pool viewed as 3-D (64 elems, 64*S rows, NB*Hkv pages)
-// with a box of one whole page and the 128-byte swizzle.
+// Tensor map over a page pool viewed as 3-D (one 128-byte stick of elements,
+// 64*S stick rows, NB*Hkv pages) with a box of one whole page and the 128-byte
+// swizzle.  elem_bytes 2: fp16 pages (64-element sticks, S = D/64);
+// elem_bytes 1: fp8 pages (128-element sticks, S = D/128).
 int make_page_pool_map(CUtensorMap *map, const void *pool, int64_t num_blocks,
-                       int64_t num_kv_heads);
+                       int64_t num_kv_heads, int elem_bytes = 2);
 
 // --------------------------------------------------------------- device ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

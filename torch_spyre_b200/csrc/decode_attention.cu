@@ -52,7 +52,8 @@ static int decode_entry(
     int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq,
     float scale, int64_t num_splits, void *workspace, int64_t workspace_bytes,
     int32_t *error_flag, void *stream, const void *k_new, const void *v_new, int64_t new_sb,
-    int64_t new_sh, bool append) {
+    int64_t new_sh, bool append, bool fp8 = false, const void *k_scale = nullptr,
+    const void *v_scale = nullptr) {
   clear_error();
   B200KV_CHECK_ARG(batch >= 0, "batch must be >= 0");
   B200KV_CHECK_ARG(num_q_heads > 0 && num_kv_heads > 0, "head counts must be > 0");
@@ -101,10 +102,15 @@ static int decode_entry(
     if (use_simt_kernel())
       return set_error(B200KV_ERR_UNSUPPORTED, "fused append needs the tensor-core kernel");
   }
+  if (fp8) {
+    B200KV_CHECK_ARG(k_scale && v_scale, "k_scale / v_scale must not be null");
+    if (use_simt_kernel())
+      return set_error(B200KV_ERR_UNSUPPORTED, "fp8 pages need the tensor-core kernel");
+  }
   CUtensorMap km, vm;
-  int st = make_page_pool_map(&km, k_pool, num_blocks, num_kv_heads);
+  int st = make_page_pool_map(&km, k_pool, num_blocks, num_kv_heads, fp8 ? 1 : 2);
   if (st != B200KV_OK) return st;
-  st = make_page_pool_map(&vm, v_pool, num_blocks, num_kv_heads);
+  st = make_page_pool_map(&vm, v_pool, num_blocks, num_kv_heads, fp8 ? 1 : 2);
   if (st != B200KV_OK) return st;
 
   DecodeArgs a;
@@ -137,6 +143,14 @@ static int decode_entry(
     a.new_sh = new_sh;
     a.k_pool_w = static_cast<__half *>(const_cast<void *>(k_pool));
     a.v_pool_w = static_cast<__half *>(const_cast<void *>(v_pool));
+  }
+  if (fp8) {
+    a.k_scale = static_cast<const __half *>(k_scale);
+    a.v_scale = static_cast<const __half *>(v_scale);
+    if (append) {
+      a.k_pool8_w = static_cast<uint8_t *>(const_cast<void *>(k_pool));
+      a.v_pool8_w = static_cast<uint8_t *>(const_cast<void *>(v_pool));
+    }
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_simt_kernel()) {
@@ -175,4 +189,34 @@ extern "C" int b200kv_decode_attention_append_f16(
                       num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
                       workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
                       new_stride_h, true);
+}
+
+extern "C" int b200kv_decode_attention_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool, const void *v_pool,
+    const void *k_scale, const void *v_scale, const int32_t *block_table,
+    int64_t block_table_stride, const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq, float scale,
+    int64_t num_splits, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream) {
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, nullptr, nullptr, 0, 0, false,
+                      true, k_scale, v_scale);
+}
+
+extern "C" int b200kv_decode_attention_append_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new, const void *v_new,
+    int64_t new_stride_b, int64_t new_stride_h, void *k_pool, void *v_pool, const void *k_scale,
+    const void *v_scale, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b, int64_t out_stride_h,
+    float *lse, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+    int64_t num_blocks, int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
+                      new_stride_h, true, true, k_scale, v_scale);
 }

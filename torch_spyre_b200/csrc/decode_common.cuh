@@ -41,6 +41,11 @@ struct DecodeArgs {
   const __half *k_new = nullptr, *v_new = nullptr;
   int64_t new_sb = 0, new_sh = 0;
   __half *k_pool_w = nullptr, *v_pool_w = nullptr;
+  // FP8 pages (null for fp16 pages): the pools hold e4m3 values whose fp16
+  // dequantisation scales are *k_scale / *v_scale; the fused append writes the
+  // quantised new rows through k_pool8_w / v_pool8_w.
+  const __half *k_scale = nullptr, *v_scale = nullptr;
+  uint8_t *k_pool8_w = nullptr, *v_pool8_w = nullptr;
 };
 
 struct WorkspaceLayout {

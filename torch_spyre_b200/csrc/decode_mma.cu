@@ -32,7 +32,22 @@
 //             output (unsplit pair) or the fp32 partial, takes the pair's
 //             completion ticket and, holding the last one, merges the pair's
 //             partials (online log-sum-exp, decode_common.cuh).
+//
+// FP8 pages (kFp8): the pools hold e4m3 values, one 128-byte stick per token
+// row (8 KiB pages).  The consumers widen them to fp16 in registers (exact) and
+// run the same fp16 MMAs; because both contractions are sums, the order of
+// their reduction index inside a fragment is free:
+//   K: ldmatrix on the fp8 rows gives lane (r, j) bytes d = 4j..4j+3 of a
+//      16-byte chunk; they serve as fragment columns k = 2j, 2j+1 (low pair)
+//      and 2j+8, 2j+9 (high pair), and the Q^T fragment is loaded with the
+//      same order (fp16 elements 4j..4j+3 of the chunk);
+//   V: ldmatrix.trans of the b16 view gives lane (i, j) tokens 2j, 2j+1 of
+//      dims 2i, 2i+1; a byte permute splits them into dims 2i (fragment row
+//      i) and 2i+1 (row i + 8), so O^T row r of m-tile mt is d = 16 mt + 2r
+//      and row r + 8 is d = 16 mt + 2r + 1.
+// The K scale folds into the softmax scale, the V scale into the epilogue.
 #include "decode_kernels.h"
+#include "fp8.cuh"
 
 namespace b200kv {
 namespace {
@@ -59,9 +74,10 @@ constexpr int kPieceHdr = kPieceML + kConsumerWarps * 8 * 8;
 constexpr int kPieceBytes = (kPieceHdr + 64 + 127) & ~127;
 constexpr int kPieceBufs = 2;
 
-template <int NST>
+template <int NST, bool kFp8>
 struct MmaSmem {
-  static constexpr int kStageBytes = 2 * kPageBytes;                     // K page + V page
+  static constexpr int kPage = kFp8 ? kPageBytesFp8 : kPageBytes;
+  static constexpr int kStageBytes = 2 * kPage;                          // K page + V page
   static constexpr int kQ = NST * kStageBytes;                           // q slot per stage
   static constexpr int kPiece = kQ + NST * kQSlotBytes;                  // piece buffers
   static constexpr int kNew = kPiece + kPieceBufs * kPieceBytes;         // new K+V row per stage
@@ -106,6 +122,9 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
+// e4m3 pair (bytes 0, 1 of x) -> fp16x2 for an MMA fragment register
+__device__ __forceinline__ uint32_t f8lo(uint32_t x) { return e4m3x2_to_half2(x); }
+__device__ __forceinline__ uint32_t f8hi(uint32_t x) { return e4m3x2_to_half2(x >> 16); }
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t *>(&h);
@@ -130,12 +149,12 @@ __device__ __forceinline__ float quad_sum(float v) {
   return v + __shfl_xor_sync(0xffffffffu, v, 16);
 }
 
-template <int G, int NST, bool kAppend>
+template <int G, int NST, bool kAppend, bool kFp8>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
   static_assert(G >= 1 && G <= 8, "the head group sits in one n = 8 MMA tile");
-  using L = MmaSmem<NST>;
+  using L = MmaSmem<NST, kFp8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -212,7 +231,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               if (kAppend) d.blk = (raw >= 0 && raw < a.num_blocks) ? raw : -1;
               d.flags = (i == 0 ? kDescFirst : 0) | (i == nstages - 1 ? kDescLast : 0) |
                         (has ? kDescPage : 0) | (app ? kDescNew : 0);
-              uint32_t tx = has ? 2 * kPageBytes : 0;
+              uint32_t tx = has ? 2 * L::kPage : 0;
               if (has && i == 0) tx += G * kHeadDim * 2;
               if (app) tx += 2 * kHeadDim * 2;
               mbar_arrive_expect_tx(&full[stage], tx);
@@ -233,7 +252,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                 uint8_t *dst = smem + stage * L::kStageBytes;
                 const int page = blk * a.hkv + pc.kvh;
                 tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
-                tma_load_3d(dst + kPageBytes, &vmap, &full[stage], 0, 0, page, policy);
+                tma_load_3d(dst + L::kPage, &vmap, &full[stage], 0, 0, page, policy);
               }
             }
             if (++stage == NST) {
@@ -260,6 +279,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   // partials.  Runs beside the consumers, which never wait for it unless it
   // falls two pieces behind.
   if (warp == kEpilogueWarp) {
+    const float vsc = kFp8 ? __half2float(*a.v_scale) : 1.f;  // V dequantisation scale
     for (int k = 0;; ++k) {
       const int pb = k & 1;
       mbar_wait_bounded(&pfull[pb], (k >> 1) & 1, a.error_flag);
@@ -287,7 +307,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 #pragma unroll
           for (int w = 0; w < kConsumerWarps; ++w)
             x = fmaf(wo[(w * kHeadDim + lane + 32 * kk) * 8 + g], sw[w], x);
-          acc[g][kk] = x;
+          acc[g][kk] = kFp8 ? x * vsc : x;
         }
         mx[g] = m;
         ls[g] = l;
@@ -340,7 +360,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   const int qh = lane >> 2;          // head of this lane's Q^T fragment (n index)
   const int hc = (lane & 3) * 2;     // heads of this lane's accumulator columns
   const int tr = t0 + (lane >> 2);   // token of this lane's S^T rows (and +8)
-  const float sc = a.scale_log2;
+  const int k_chunk8 = mi >> 1;      // fp8 pages: 16-byte chunk (of a pair) this lane addresses
+  const float sc = kFp8 ? a.scale_log2 * __half2float(*a.k_scale) : a.scale_log2;
+  __half2 kinv = {}, vinv = {};      // fp8 fused append: quantisation scales of the new rows
+  if (kFp8 && kAppend) {
+    kinv = fp8_inv_scale2(*a.k_scale);
+    vinv = fp8_inv_scale2(*a.v_scale);
+  }
 
   // Hands this warp's state of the finished piece (or the end marker) to the
   // epilogue through piece buffer k & 1.
@@ -356,12 +382,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         wml[warp * 8 + hc] = make_float2(m0, l0);
         wml[warp * 8 + hc + 1] = make_float2(m1, l1);
       }
+      // accumulator rows of m-tile mt: d = 16 mt + r and + 8 (fp16 pages),
+      // d = 16 mt + 2r and + 1 (fp8 pages), r = lane / 4
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
-        const int dd = mt * 16 + (lane >> 2);
+        const int dd = mt * 16 + (kFp8 ? 2 * (lane >> 2) : (lane >> 2));
         float *w = wo + (warp * kHeadDim + dd) * 8 + hc;
         *reinterpret_cast<float2 *>(w) = make_float2(o[mt][0], o[mt][1]);
-        *reinterpret_cast<float2 *>(w + 8 * 8) = make_float2(o[mt][2], o[mt][3]);
+        *reinterpret_cast<float2 *>(w + (kFp8 ? 8 : 8 * 8)) = make_float2(o[mt][2], o[mt][3]);
       }
     }
     if (warp == 0 && lane == 0) {
@@ -392,20 +420,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const bool first = d.flags & kDescFirst, last = d.flags & kDescLast;
     const bool has = d.flags & kDescPage;
     const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
-    const uint32_t vbase = kbase + kPageBytes;
+    const uint32_t vbase = kbase + L::kPage;
     if (first) {
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
       m0 = m1 = -CUDART_INF_F;
       l0 = l1 = 0.f;
       if (has) {  // q of this piece, staged with its first page
-        const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes + hc * 2;
+        // fragment columns 2j, 2j+1 / 2j+8, 2j+9 of each 16-dim step are dims
+        // 2j, 2j+1 / 2j+8, 2j+9 (fp16 pages) or 4j..4j+3 (fp8 pages)
+        const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes +
+                            (kFp8 ? 4 * (lane & 3) : hc) * 2;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           uint32_t x0 = 0u, x1 = 0u;
           if (qh < G) {
             asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x0) : "r"(qs + ks * 32));
-            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x1) : "r"(qs + ks * 32 + 16));
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x1) : "r"(qs + ks * 32 + (kFp8 ? 4 : 16)));
           }
           qb[ks][0] = x0;
           qb[ks][1] = x1;
@@ -420,6 +451,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         const int kv = lane >> 4;
         const uint8_t *src = smem + L::kNew + stage * 2 * kHeadDim * 2 + kv * kHeadDim * 2 + c * 16;
         const uint4 v = *reinterpret_cast<const uint4 *>(src);
+        if (kFp8) {  // quantise: dims 8c..8c+7 are bytes 8c..8c+7 of the page row
+          const uint2 q8 = quantize8_e4m3(v, kv ? vinv : kinv);
+          *reinterpret_cast<uint2 *>(smem + stage * L::kStageBytes + kv * L::kPage +
+                                     swz_off(0, t_new, c >> 1) + (c & 1) * 8) = q8;
+          if (d.blk >= 0) {
+            uint8_t *pool = kv ? a.v_pool8_w : a.k_pool8_w;
+            const int64_t off = ((static_cast<int64_t>(d.blk) * a.hkv + d.kvh) * kPageTokens + t_new) *
+                                    kHeadDim + c * 8;
+            *reinterpret_cast<uint2 *>(pool + off) = q8;
+          }
+        } else {
         *reinterpret_cast<uint4 *>(smem + stage * L::kStageBytes + kv * kPageBytes +
                                    swz_off(c >> 3, t_new, c & 7)) = v;
         if (d.blk >= 0) {
@@ -429,6 +471,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
                               t_new * kStickElems + (c & 7) * 8;
           *reinterpret_cast<uint4 *>(pool + off) = v;
         }
+        }
         wrote_smem = true;
       }
       __syncwarp();
@@ -437,14 +480,33 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const int valid = min(kPageTokens, d.ctx - d.page * kPageTokens);
       const bool partial = valid < t0 + 16;
       if (partial) {  // zero this warp's V rows past the context (0 * NaN = NaN in the MMA)
-        for (int idx = lane; idx < 16 * 16; idx += 32) {
-          const int t = t0 + (idx >> 4), cc = idx & 15;
-          if (t >= valid) st_shared_zero16(vbase + swz_off(cc >> 3, t, cc & 7));
+        if (kFp8) {
+          for (int idx = lane; idx < 16 * 8; idx += 32) {
+            const int t = t0 + (idx >> 3), cc = idx & 7;
+            if (t >= valid) st_shared_zero16(vbase + swz_off(0, t, cc));
+          }
+        } else {
+          for (int idx = lane; idx < 16 * 16; idx += 32) {
+            const int t = t0 + (idx >> 4), cc = idx & 15;
+            if (t >= valid) st_shared_zero16(vbase + swz_off(cc >> 3, t, cc & 7));
+          }
         }
         __syncwarp();
       }
       // S^T = K . Q^T over the 128 dims (two independent accumulation chains)
       float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+      if (kFp8) {
+        // one ldmatrix.x4 = 16 tokens x 32 dims: chunk pair 2cc, 2cc+1
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t x[4];
+          ldsm_x4(kbase + swz_off(0, k_row, 2 * cc + k_chunk8), x);
+          const uint32_t ka[4] = {f8lo(x[0]), f8lo(x[1]), f8hi(x[0]), f8hi(x[1])};
+          const uint32_t kb[4] = {f8lo(x[2]), f8lo(x[3]), f8hi(x[2]), f8hi(x[3])};
+          mma16816(s, ka, qb[2 * cc][0], qb[2 * cc][1]);
+          mma16816(s2, kb, qb[2 * cc + 1][0], qb[2 * cc + 1][1]);
+        }
+      } else {
 #pragma unroll
       for (int ks = 0; ks < 8; ks += 2) {
         uint32_t ka[4], kb[4];
@@ -453,6 +515,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         ldsm_x4(kbase + swz_off((dd + 16) >> 6, k_row, ((dd + 16) & 63) >> 3), kb);
         mma16816(s, ka, qb[ks][0], qb[ks][1]);
         mma16816(s2, kb, qb[ks + 1][0], qb[ks + 1][1]);
+      }
       }
       // online softmax over this warp's 16 tokens, heads hc and hc + 1
       const float x0 = tr < valid ? (s[0] + s2[0]) * sc : -CUDART_INF_F;
@@ -486,12 +549,29 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the warp
       const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
       // O^T += V^T . P^T, 8 tiles of 16 dims
+      if (kFp8) {
+        // ldmatrix.trans (b16 view) of tokens 0-7 / 8-15 x chunk pair 2cc, 2cc+1;
+        // byte permute {t2j d2i, t2j d2i+1, t2j+1 d2i, t2j+1 d2i+1} ->
+        // {d2i: t2j, t2j+1 | d2i+1: t2j, t2j+1}
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t x[4];
+          ldsm_x4_t(vbase + swz_off(0, k_row, 2 * cc + k_chunk8), x);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) x[i] = __byte_perm(x[i], 0u, 0x3120);
+          const uint32_t va[4] = {f8lo(x[0]), f8hi(x[0]), f8lo(x[1]), f8hi(x[1])};
+          const uint32_t vb[4] = {f8lo(x[2]), f8hi(x[2]), f8lo(x[3]), f8hi(x[3])};
+          mma16816(o[2 * cc], va, pb0, pb1);
+          mma16816(o[2 * cc + 1], vb, pb0, pb1);
+        }
+      } else {
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         const int dd = mt * 16 + v_dof;
         uint32_t va[4];
         ldsm_x4_t(vbase + swz_off(dd >> 6, v_row, (dd & 63) >> 3), va);
         mma16816(o[mt], va, pb0, pb1);
+      }
       }
       if (partial || wrote_smem) fence_proxy_async_smem();  // st.shared before the next TMA write
     }
@@ -505,12 +585,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
 }
 
-template <int G, int NST, bool kAppend>
+template <int G, int NST, bool kAppend, bool kFp8>
 int launch_mma_impl(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
                     cudaStream_t stream) {
-  using L = MmaSmem<NST>;
+  using L = MmaSmem<NST, kFp8>;
   static_assert(L::kAlloc <= 227 * 1024, "shared memory budget");
-  auto kern = decode_mma_kernel<G, NST, kAppend>;
+  auto kern = decode_mma_kernel<G, NST, kAppend, kFp8>;
   int dev = 0, sms = 0;
   int st = current_device_sm_count(&dev, &sms);
   if (st != B200KV_OK) return st;
@@ -536,27 +616,35 @@ int launch_mma_impl(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a,
   return B200KV_OK;
 }
 
-template <int G, int NST>
-int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
-               cudaStream_t stream) {
-  if (a.k_new != nullptr) return launch_mma_impl<G, NST, true>(km, vm, a, partitions, stream);
-  return launch_mma_impl<G, NST, false>(km, vm, a, partitions, stream);
-}
-
 #ifndef B200KV_MMA_STAGES
 #define B200KV_MMA_STAGES 5
 #endif
-constexpr int kMmaStages = B200KV_MMA_STAGES;  // 5 stages (160 KiB) fit beside the q slots
+#ifndef B200KV_MMA_STAGES_FP8
+#define B200KV_MMA_STAGES_FP8 8
+#endif
+constexpr int kMmaStages = B200KV_MMA_STAGES;        // fp16: 5 stages (160 KiB) beside the q slots
+constexpr int kMmaStagesFp8 = B200KV_MMA_STAGES_FP8; // fp8: 8 stages (128 KiB)
+
+template <int G>
+int launch_mma(const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a, int partitions,
+               cudaStream_t stream) {
+  const bool app = a.k_new != nullptr;
+  if (a.k_scale != nullptr)
+    return app ? launch_mma_impl<G, kMmaStagesFp8, true, true>(km, vm, a, partitions, stream)
+               : launch_mma_impl<G, kMmaStagesFp8, false, true>(km, vm, a, partitions, stream);
+  return app ? launch_mma_impl<G, kMmaStages, true, false>(km, vm, a, partitions, stream)
+             : launch_mma_impl<G, kMmaStages, false, false>(km, vm, a, partitions, stream);
+}
 
 }  // namespace
 
 int launch_decode_mma(int group, const CUtensorMap &km, const CUtensorMap &vm, DecodeArgs &a,
                       int partitions, cudaStream_t stream) {
   switch (group) {
-    case 1: return launch_mma<1, kMmaStages>(km, vm, a, partitions, stream);
-    case 2: return launch_mma<2, kMmaStages>(km, vm, a, partitions, stream);
-    case 4: return launch_mma<4, kMmaStages>(km, vm, a, partitions, stream);
-    case 8: return launch_mma<8, kMmaStages>(km, vm, a, partitions, stream);
+    case 1: return launch_mma<1>(km, vm, a, partitions, stream);
+    case 2: return launch_mma<2>(km, vm, a, partitions, stream);
+    case 4: return launch_mma<4>(km, vm, a, partitions, stream);
+    case 8: return launch_mma<8>(km, vm, a, partitions, stream);
     default: return set_error(B200KV_ERR_UNSUPPORTED, "group %d", group);
   }
 }

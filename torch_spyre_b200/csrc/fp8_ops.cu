@@ -1,0 +1,169 @@
+// FP8 (e4m3) quantize / dequantize with a pre-computed fp16 scale, and the KV
+// append into fp8 pages (quantize on write).
+//
+// Reference behaviour replaced:
+//   quantize    spyre::quantize_fp8_with_scale (torch_spyre/_inductor/
+//               customops.py:587-621), decomposed as reciprocal -> multiply ->
+//               clamp(+-448) -> qfp8ch (decompositions.py:897-904);
+//   dequantize  spyre::dequantize_fp8_with_scale (customops.py:624-653),
+//               decomposed as .to(float16) * scale (decompositions.py:846-858);
+//   append      spyre::overwrite / the aten.index_copy.out fallback
+//               (customops.py:262-308, ops/fallbacks.py:237-259) into a cache
+//               whose pages hold e4m3 values.
+// All three are HBM-bound streams: 16-byte fp16 vectors against 8-byte e4m3
+// vectors, one thread per 8 elements, grid-stride.
+#include "fp8.cuh"
+
+namespace b200kv {
+namespace {
+
+// Per-row scale of a [rows, cols] tensor: scale[row * scale_stride].
+template <bool kQuant>
+__global__ void __launch_bounds__(256) fp8_convert_kernel(const void *__restrict__ src,
+                                                          void *__restrict__ dst, int64_t rows,
+                                                          int64_t cols,
+                                                          const __half *__restrict__ scale,
+                                                          int64_t scale_stride, int vec) {
+  const int64_t step = int64_t(gridDim.x) * blockDim.x;
+  if (vec) {  // cols % 8 == 0, buffers aligned: one 8-element vector per thread
+    const int64_t per_row = cols / 8;
+    const int64_t total = rows * per_row;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += step) {
+      const int64_t r = i / per_row;
+      const __half s = scale[r * scale_stride];
+      if (kQuant) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(src) + i);
+        __stcs(reinterpret_cast<uint2 *>(dst) + i, quantize8_e4m3(v, fp8_inv_scale2(s)));
+      } else {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(src) + i);
+        __stcs(reinterpret_cast<uint4 *>(dst) + i, dequantize8_e4m3(v, __half2half2(s)));
+      }
+    }
+    return;
+  }
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += step) {
+    const __half s = scale[(i / cols) * scale_stride];
+    if (kQuant) {
+      const uint32_t x = reinterpret_cast<const uint16_t *>(src)[i];
+      reinterpret_cast<uint8_t *>(dst)[i] =
+          static_cast<uint8_t>(quantize2_e4m3(x, fp8_inv_scale2(s)) & 0xffu);
+    } else {
+      const uint32_t h = e4m3x2_to_half2(reinterpret_cast<const uint8_t *>(src)[i]);
+      const __half y = __hmul(*reinterpret_cast<const __half *>(&h), s);
+      reinterpret_cast<__half *>(dst)[i] = y;
+    }
+  }
+}
+
+constexpr int kChunks = kHeadDim / 8;  // 8-element chunks per head row (16)
+
+// One thread per (token, head, 8-element chunk); K and V by the same thread.
+// fp8 page (D = 128): byte offset page * 8192 + slot * 128 + d.
+__global__ void __launch_bounds__(256) kv_append_fp8_kernel(
+    const __half *__restrict__ k_new, const __half *__restrict__ v_new, int64_t stride_n,
+    int64_t stride_h, uint8_t *__restrict__ k_pool, uint8_t *__restrict__ v_pool,
+    const __half *__restrict__ k_scale, const __half *__restrict__ v_scale,
+    const int64_t *__restrict__ slots, int64_t num_tokens, int num_kv_heads, int64_t num_slots,
+    int32_t *error_flag) {
+  const __half2 kinv = fp8_inv_scale2(*k_scale), vinv = fp8_inv_scale2(*v_scale);
+  const int64_t total = num_tokens * num_kv_heads * kChunks;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % kChunks);
+    const int64_t nh = i / kChunks;
+    const int h = static_cast<int>(nh % num_kv_heads);
+    const int64_t n = nh / num_kv_heads;
+    const int64_t slot = __ldg(slots + n);
+    if (slot < 0) continue;  // padding token
+    if (slot >= num_slots) {
+      if (error_flag && c == 0 && h == 0) atomicOr(error_flag, B200KV_DEVERR_BAD_SLOT);
+      continue;
+    }
+    const int64_t page = (slot >> 6) * num_kv_heads + h;
+    const int64_t dst = (page * kPageTokens + (slot & 63)) * kHeadDim + c * 8;
+    const int64_t src = n * stride_n + h * stride_h + c * 8;
+    const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(k_new + src));
+    const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(v_new + src));
+    *reinterpret_cast<uint2 *>(k_pool + dst) = quantize8_e4m3(kv, kinv);
+    *reinterpret_cast<uint2 *>(v_pool + dst) = quantize8_e4m3(vv, vinv);
+  }
+}
+
+int grid_for(int64_t work_items, int threads) {
+  int dev = 0, sms = 0;
+  if (current_device_sm_count(&dev, &sms) != B200KV_OK) return -1;
+  const int64_t want = (work_items + threads - 1) / threads;
+  const int64_t cap = int64_t(sms) * 8;  // 8 resident 256-thread CTAs per SM
+  return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+bool aligned(const void *p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int convert_entry(bool quant, const void *x, void *out, int64_t rows, int64_t cols,
+                  const void *scale, int64_t scale_stride, void *stream) {
+  clear_error();
+  B200KV_CHECK_ARG(rows >= 0 && cols >= 0, "rows and cols must be >= 0");
+  B200KV_CHECK_ARG(scale_stride >= 0, "scale_stride must be >= 0");
+  if (rows == 0 || cols == 0) return B200KV_OK;
+  B200KV_CHECK_ARG(x && out && scale, "null pointer argument");
+  const int vec = (cols % 8 == 0 && aligned(x, quant ? 16 : 8) && aligned(out, quant ? 8 : 16)) ? 1 : 0;
+  const int grid = grid_for(vec ? rows * (cols / 8) : rows * cols, 256);
+  if (grid < 0) return B200KV_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __half *sc = static_cast<const __half *>(scale);
+  if (quant)
+    fp8_convert_kernel<true><<<grid, 256, 0, s>>>(x, out, rows, cols, sc, scale_stride, vec);
+  else
+    fp8_convert_kernel<false><<<grid, 256, 0, s>>>(x, out, rows, cols, sc, scale_stride, vec);
+  B200KV_CUDA_TRY(cudaGetLastError());
+  return B200KV_OK;
+}
+
+}  // namespace
+}  // namespace b200kv
+
+using namespace b200kv;
+
+extern "C" int b200kv_quantize_fp8_f16(const void *x, void *out, int64_t rows, int64_t cols,
+                                       const void *scale, int64_t scale_stride, void *stream) {
+  return convert_entry(true, x, out, rows, cols, scale, scale_stride, stream);
+}
+
+extern "C" int b200kv_dequantize_fp8_f16(const void *x, void *out, int64_t rows, int64_t cols,
+                                         const void *scale, int64_t scale_stride, void *stream) {
+  return convert_entry(false, x, out, rows, cols, scale, scale_stride, stream);
+}
+
+extern "C" int b200kv_kv_append_fp8(const void *k_new, const void *v_new, int64_t new_stride_n,
+                                    int64_t new_stride_h, void *k_pool, void *v_pool,
+                                    const void *k_scale, const void *v_scale,
+                                    const int64_t *slot_mapping, int64_t num_tokens,
+                                    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+                                    int32_t *error_flag, void *stream) {
+  clear_error();
+  B200KV_CHECK_ARG(num_tokens >= 0, "num_tokens must be >= 0 (got %lld)", (long long)num_tokens);
+  B200KV_CHECK_ARG(num_kv_heads > 0 && num_blocks > 0, "num_kv_heads and num_blocks must be > 0");
+  if (head_dim != kHeadDim)
+    return set_error(B200KV_ERR_UNSUPPORTED, "head_dim %lld unsupported (only %d)",
+                     (long long)head_dim, kHeadDim);
+  if (num_tokens == 0) return B200KV_OK;
+  B200KV_CHECK_ARG(k_new && v_new && k_pool && v_pool && slot_mapping && k_scale && v_scale,
+                   "null pointer argument");
+  B200KV_CHECK_ARG(aligned(k_new, 16) && aligned(v_new, 16) && aligned(k_pool, 16) &&
+                       aligned(v_pool, 16),
+                   "buffers must be 16-byte aligned");
+  B200KV_CHECK_ARG(new_stride_n % 8 == 0 && new_stride_h % 8 == 0 && new_stride_h >= kHeadDim &&
+                       new_stride_n >= 0,
+                   "new-row strides must be multiples of 8 elements (got %lld, %lld)",
+                   (long long)new_stride_n, (long long)new_stride_h);
+  const int grid = grid_for(num_tokens * num_kv_heads * kChunks, 256);
+  if (grid < 0) return B200KV_ERR_CUDA;
+  kv_append_fp8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half *>(k_new), static_cast<const __half *>(v_new), new_stride_n,
+      new_stride_h, static_cast<uint8_t *>(k_pool), static_cast<uint8_t *>(v_pool),
+      static_cast<const __half *>(k_scale), static_cast<const __half *>(v_scale), slot_mapping,
+      num_tokens, static_cast<int>(num_kv_heads), num_blocks * kPageTokens, error_flag);
+  B200KV_CUDA_TRY(cudaGetLastError());
+  return B200KV_OK;
+}

@@ -32,6 +32,7 @@ _ELEM_BYTES = {
     torch.int64: 8,
     torch.int8: 1,
     torch.uint8: 1,
+    torch.float8_e4m3fn: 1,
 }
 
 

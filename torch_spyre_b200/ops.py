@@ -89,6 +89,16 @@ def _check_pool(pool: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+def _is_fp8(pool: torch.Tensor) -> bool:
+    return pool.dtype == torch.float8_e4m3fn
+
+
+def _need(t: Optional[torch.Tensor], name: str) -> torch.Tensor:
+    if t is None:
+        raise ValueError(f"fp8 pools need {name} (their fp16 dequantisation scale)")
+    return t
+
+
 # --------------------------------------------------------- decode attention --
 @torch.library.custom_op("b200kv::decode_attention", mutates_args=(), device_types="cuda")
 def _decode_attention_op(
@@ -162,18 +172,29 @@ def decode_attention(
     num_splits: int = 0,
     return_lse: bool = False,
     error_flag: Optional[torch.Tensor] = None,
+    k_scale: Optional[torch.Tensor] = None,
+    v_scale: Optional[torch.Tensor] = None,
 ):
     """Decode attention of one new token per sequence over the paged KV pools.
 
-    q [B, Hq, D] fp16; pools fp16 [NB, Hkv, D/64, 64, 64]; block_table int32
+    q [B, Hq, D] fp16; pools fp16 [NB, Hkv, D/64, 64, 64], or float8_e4m3fn
+    [NB, Hkv, D/128, 64, 128] with their fp16 dequantisation scales
+    ``k_scale`` / ``v_scale`` (one-element device tensors); block_table int32
     [B, max_blocks]; context_lens int32 [B].  Returns out [B, Hq, D] fp16 (and
     the natural-log LSE [B, Hq] fp32 when ``return_lse``).
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    out, lse = torch.ops.b200kv.decode_attention(
-        q, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
-    )
+    if _is_fp8(k_pool):
+        from . import fp8  # noqa: F401  (registers the fp8 ops)
+        out, lse = torch.ops.b200kv.decode_attention_fp8(
+            q, k_pool, v_pool, _need(k_scale, "k_scale"), _need(v_scale, "v_scale"), block_table, context_lens,
+            float(scale), int(num_splits), error_flag
+        )
+    else:
+        out, lse = torch.ops.b200kv.decode_attention(
+            q, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
+        )
     return (out, lse) if return_lse else out
 
 
@@ -249,18 +270,28 @@ def decode_attention_append(
     num_splits: int = 0,
     return_lse: bool = False,
     error_flag: Optional[torch.Tensor] = None,
+    k_scale: Optional[torch.Tensor] = None,
+    v_scale: Optional[torch.Tensor] = None,
 ):
     """Appends the new token's K/V rows ([B, Hkv, D], at position
     context_lens[b] - 1) to the pools and decodes, in one launch.
 
     Same result as ``kv_append`` at those slots followed by
     ``decode_attention`` (the HF ``index_copy_`` + SDPA step of the reference).
+    fp8 pools take ``k_scale`` / ``v_scale``; the new rows are quantized.
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    out, lse = torch.ops.b200kv.decode_attention_append(
-        q, k_new, v_new, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
-    )
+    if _is_fp8(k_pool):
+        from . import fp8  # noqa: F401
+        out, lse = torch.ops.b200kv.decode_attention_append_fp8(
+            q, k_new, v_new, k_pool, v_pool, _need(k_scale, "k_scale"), _need(v_scale, "v_scale"), block_table,
+            context_lens, float(scale), int(num_splits), error_flag
+        )
+    else:
+        out, lse = torch.ops.b200kv.decode_attention_append(
+            q, k_new, v_new, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
+        )
     return (out, lse) if return_lse else out
 
 
@@ -300,8 +331,14 @@ def _(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag):
     return None
 
 
-def kv_append(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag=None) -> None:
-    """Writes row n of k_new / v_new ([N, Hkv, D]) into slot slot_mapping[n]."""
+def kv_append(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag=None, k_scale=None, v_scale=None) -> None:
+    """Writes row n of k_new / v_new ([N, Hkv, D]) into slot slot_mapping[n]
+    (quantized with k_scale / v_scale when the pools are fp8)."""
+    if _is_fp8(k_pool):
+        from . import fp8  # noqa: F401
+        torch.ops.b200kv.kv_append_fp8(k_new, v_new, k_pool, v_pool, _need(k_scale, "k_scale"),
+                                       _need(v_scale, "v_scale"), slot_mapping, error_flag)
+        return
     torch.ops.b200kv.kv_append(k_new, v_new, k_pool, v_pool, slot_mapping, error_flag)
 
 

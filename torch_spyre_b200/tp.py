@@ -86,15 +86,21 @@ def tp_decode_step(
     group=None,
     out: Optional[torch.Tensor] = None,
     attn_fn: Optional[AttnFn] = None,
+    k_scale: Optional[torch.Tensor] = None,
+    v_scale: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """One rank's step: local decode -> o_proj partial -> SUM all-reduce.
 
     attn_fn defaults to the CUDA decode op; tests on CPU ranks pass the oracle.
+    k_scale / v_scale are the dequantisation scales of fp8 pools.
     Every rank must call this in the same order (it contains one collective).
     """
     if attn_fn is None:
         from .ops import decode_attention as attn_fn
-    attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens)
+    if k_scale is not None:
+        attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens, k_scale=k_scale, v_scale=v_scale)
+    else:
+        attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens)
     B = attn.shape[0]
     flat = attn.reshape(B, -1)
     if out is not None:

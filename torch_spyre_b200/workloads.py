@@ -101,11 +101,14 @@ class DecodeInputs:
     context_lens: torch.Tensor
     ctx: list[int] = field(default_factory=list)
 
+    k_scale: Optional[torch.Tensor] = None  # fp8 pools: fp16 dequantisation scales
+    v_scale: Optional[torch.Tensor] = None
+
     @property
     def kv_bytes(self) -> int:
         """Algorithmic KV bytes one decode step reads (K and V, valid tokens)."""
-        hkv, d = self.k_pool.shape[1], self.k_pool.shape[2] * 64
-        return sum(self.ctx) * hkv * d * 2 * 2
+        hkv, d = self.k_pool.shape[1], self.k_pool.shape[2] * self.k_pool.shape[4]
+        return sum(self.ctx) * hkv * d * 2 * self.k_pool.element_size()
 
     @property
     def step_bytes(self) -> int:
@@ -162,3 +165,22 @@ def make_decode_inputs(
         context_lens=torch.tensor(ctx, dtype=torch.int32, device=device),
         ctx=ctx,
     )
+
+
+# Scale of the seeded fp8 pools: N(0, 1) values stay inside e4m3's +-448 range
+# up to 7 sigma (1/64 is exact in fp16).
+KV_FP8_SCALE = 1.0 / 64
+
+
+def quantize_decode_inputs(inp: DecodeInputs, k_scale: float = KV_FP8_SCALE,
+                           v_scale: float = KV_FP8_SCALE) -> DecodeInputs:
+    """The same step with its pools quantized to fp8 pages (on the pools'
+    device, by the library's quantize kernel)."""
+    from .fp8 import quantize_pool
+
+    dev = inp.k_pool.device
+    ks = torch.tensor([k_scale], dtype=torch.float16, device=dev)
+    vs = torch.tensor([v_scale], dtype=torch.float16, device=dev)
+    return DecodeInputs(q=inp.q, k_pool=quantize_pool(inp.k_pool, ks), v_pool=quantize_pool(inp.v_pool, vs),
+                        block_table=inp.block_table, context_lens=inp.context_lens, ctx=list(inp.ctx),
+                        k_scale=ks, v_scale=vs)
