@@ -350,22 +350,38 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   }
 
   // ----------------------------------------------------------- consumers --
-  const int t0 = warp * 16;          // this warp's 16 tokens of each page
+  // The stages are taken in turn: warp w processes the pages of stages
+  // number w, w + 4, w + 8, ... (counted from the kernel start) and passes
+  // over the others after reading their descriptors.  Each warp keeps its own
+  // online-softmax state per piece.
   const int mi = lane >> 3;          // ldmatrix: which 8x8 matrix this lane addresses
   const int mr = lane & 7;           // ldmatrix: row within that matrix
-  const int k_row = t0 + mr + (mi & 1) * 8;   // K rows (A of Q.K^T, non-transposed)
-  const int k_dof = (mi >> 1) * 8;
-  const int v_row = t0 + mr + (mi >> 1) * 8;  // V rows (A = V^T of P.V, transposed)
-  const int v_dof = (mi & 1) * 8;
   const int qh = lane >> 2;          // head of this lane's Q^T fragment (n index)
   const int hc = (lane & 3) * 2;     // heads of this lane's accumulator columns
-  const int tr = t0 + (lane >> 2);   // token of this lane's S^T rows (and +8)
-  const int k_chunk8 = mi >> 1;      // fp8 pages: 16-byte chunk (of a pair) this lane addresses
+  const int tr = lane >> 2;          // token (within a 16-token tile) of this lane's S^T rows (and +8)
   const float sc = kFp8 ? a.scale_log2 * __half2float(*a.k_scale) : a.scale_log2;
   __half2 kinv = {}, vinv = {};      // fp8 fused append: quantisation scales of the new rows
   if (kFp8 && kAppend) {
     kinv = fp8_inv_scale2(*a.k_scale);
     vinv = fp8_inv_scale2(*a.v_scale);
+  }
+  // Byte offsets, in a staged page, of this lane's ldmatrix rows.  Token tile
+  // mt (16 tokens) adds 2048 * mt: its rows share the swizzle phase (row & 7).
+  //   fp16 K (non-transposed, A of S^T = K Q^T): 16-dim step ks
+  //   fp16 V (transposed, A = V^T of O^T = V^T P^T): 16-dim tile mt
+  //   fp8 K and V: 32-dim step cc (chunk pair 2cc, 2cc + 1)
+  uint32_t koff[kFp8 ? 4 : 8], voff[kFp8 ? 4 : 8];
+  if (kFp8) {
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) koff[cc] = voff[cc] = swz_off(0, mr + (mi & 1) * 8, 2 * cc + (mi >> 1));
+  } else {
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int dk = ks * 16 + (mi >> 1) * 8;
+      koff[ks] = swz_off(dk >> 6, mr + (mi & 1) * 8, (dk & 63) >> 3);
+      const int dv = ks * 16 + (mi & 1) * 8;
+      voff[ks] = swz_off(dv >> 6, mr + (mi >> 1) * 8, (dv & 63) >> 3);
+    }
   }
 
   // Hands this warp's state of the finished piece (or the end marker) to the
@@ -408,9 +424,42 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   uint32_t qb[8][2];
   float o[8][4];
   float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
-  int stage = 0, piece = 0;
+
+  // The appended token's rows replace the staged ones (the page's warp writes
+  // them into the stage's K/V pages and into the pools).
+  auto apply_append = [&](int st, const StageDesc &dd) {
+    const int t_new = (dd.ctx - 1) % kPageTokens;
+    const int c = lane & 15;  // 16-byte chunk of the row; lanes 0-15 K, 16-31 V
+    const int kv = lane >> 4;
+    const uint8_t *src = smem + L::kNew + st * 2 * kHeadDim * 2 + kv * kHeadDim * 2 + c * 16;
+    const uint4 v = *reinterpret_cast<const uint4 *>(src);
+    if (kFp8) {  // quantise: dims 8c..8c+7 are bytes 8c..8c+7 of the page row
+      const uint2 q8 = quantize8_e4m3(v, kv ? vinv : kinv);
+      *reinterpret_cast<uint2 *>(smem + st * L::kStageBytes + kv * L::kPage + swz_off(0, t_new, c >> 1) +
+                                 (c & 1) * 8) = q8;
+      if (dd.blk >= 0) {
+        uint8_t *pool = kv ? a.v_pool8_w : a.k_pool8_w;
+        const int64_t off =
+            ((static_cast<int64_t>(dd.blk) * a.hkv + dd.kvh) * kPageTokens + t_new) * kHeadDim + c * 8;
+        *reinterpret_cast<uint2 *>(pool + off) = q8;
+      }
+    } else {
+      *reinterpret_cast<uint4 *>(smem + st * L::kStageBytes + kv * kPageBytes + swz_off(c >> 3, t_new, c & 7)) =
+          v;
+      if (dd.blk >= 0) {
+        __half *pool = kv ? a.v_pool_w : a.k_pool_w;
+        const int64_t off = ((static_cast<int64_t>(dd.blk) * a.hkv + dd.kvh) * kSticks + (c >> 3)) *
+                                (kPageTokens * kStickElems) +
+                            t_new * kStickElems + (c & 7) * 8;
+        *reinterpret_cast<uint4 *>(pool + off) = v;
+      }
+    }
+    __syncwarp();
+  };
+
+  int stage = 0, piece = 0, seq = 0;
   uint32_t phase = 0;
-  for (;;) {
+  for (;; ++seq) {
     mbar_wait_bounded(&full[stage], phase, a.error_flag);
     const StageDesc d = descs[stage];
     if (d.flags & kDescEnd) {
@@ -419,14 +468,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
     const bool first = d.flags & kDescFirst, last = d.flags & kDescLast;
     const bool has = d.flags & kDescPage;
-    const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
-    const uint32_t vbase = kbase + L::kPage;
     if (first) {
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
       m0 = m1 = -CUDART_INF_F;
       l0 = l1 = 0.f;
-      if (has) {  // q of this piece, staged with its first page
+      if (has) {  // q of this piece, staged with its first page (every warp reads it)
         // fragment columns 2j, 2j+1 / 2j+8, 2j+9 of each 16-dim step are dims
         // 2j, 2j+1 / 2j+8, 2j+9 (fp16 pages) or 4j..4j+3 (fp8 pages)
         const uint32_t qs = smem_u32(smem + L::kQ + stage * kQSlotBytes) + qh * kQRowBytes +
@@ -443,100 +490,82 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         }
       }
     }
-    bool wrote_smem = false;
-    if (kAppend && (d.flags & kDescNew)) {  // appended token: its rows replace the staged ones
-      const int t_new = (d.ctx - 1) % kPageTokens;
-      if ((t_new >> 4) == warp) {
-        const int c = lane & 15;  // 16-byte chunk of the row; lanes 0-15 K, 16-31 V
-        const int kv = lane >> 4;
-        const uint8_t *src = smem + L::kNew + stage * 2 * kHeadDim * 2 + kv * kHeadDim * 2 + c * 16;
-        const uint4 v = *reinterpret_cast<const uint4 *>(src);
-        if (kFp8) {  // quantise: dims 8c..8c+7 are bytes 8c..8c+7 of the page row
-          const uint2 q8 = quantize8_e4m3(v, kv ? vinv : kinv);
-          *reinterpret_cast<uint2 *>(smem + stage * L::kStageBytes + kv * L::kPage +
-                                     swz_off(0, t_new, c >> 1) + (c & 1) * 8) = q8;
-          if (d.blk >= 0) {
-            uint8_t *pool = kv ? a.v_pool8_w : a.k_pool8_w;
-            const int64_t off = ((static_cast<int64_t>(d.blk) * a.hkv + d.kvh) * kPageTokens + t_new) *
-                                    kHeadDim + c * 8;
-            *reinterpret_cast<uint2 *>(pool + off) = q8;
-          }
-        } else {
-        *reinterpret_cast<uint4 *>(smem + stage * L::kStageBytes + kv * kPageBytes +
-                                   swz_off(c >> 3, t_new, c & 7)) = v;
-        if (d.blk >= 0) {
-          __half *pool = kv ? a.v_pool_w : a.k_pool_w;
-          const int64_t off = ((static_cast<int64_t>(d.blk) * a.hkv + d.kvh) * kSticks + (c >> 3)) *
-                                  (kPageTokens * kStickElems) +
-                              t_new * kStickElems + (c & 7) * 8;
-          *reinterpret_cast<uint4 *>(pool + off) = v;
-        }
-        }
+    if (has && (seq & (kConsumerWarps - 1)) == warp) {  // this warp's page
+      bool wrote_smem = false;
+      if (kAppend && (d.flags & kDescNew)) {
+        apply_append(stage, d);
         wrote_smem = true;
       }
-      __syncwarp();
-    }
-    if (has) {
+      const uint32_t kbase = smem_u32(smem + stage * L::kStageBytes);
+      const uint32_t vbase = kbase + L::kPage;
       const int valid = min(kPageTokens, d.ctx - d.page * kPageTokens);
-      const bool partial = valid < t0 + 16;
-      if (partial) {  // zero this warp's V rows past the context (0 * NaN = NaN in the MMA)
-        if (kFp8) {
-          for (int idx = lane; idx < 16 * 8; idx += 32) {
-            const int t = t0 + (idx >> 3), cc = idx & 7;
-            if (t >= valid) st_shared_zero16(vbase + swz_off(0, t, cc));
-          }
-        } else {
-          for (int idx = lane; idx < 16 * 16; idx += 32) {
-            const int t = t0 + (idx >> 4), cc = idx & 15;
-            if (t >= valid) st_shared_zero16(vbase + swz_off(cc >> 3, t, cc & 7));
-          }
+      if (valid < kPageTokens) {  // zero the V rows past the context (0 * NaN = NaN in the MMA)
+        constexpr int kRowChunks = kFp8 ? 8 : 16;
+        for (int idx = valid * kRowChunks + lane; idx < kPageTokens * kRowChunks; idx += 32) {
+          const int t = idx / kRowChunks, cc = idx % kRowChunks;
+          st_shared_zero16(vbase + (kFp8 ? swz_off(0, t, cc) : swz_off(cc >> 3, t, cc & 7)));
         }
         __syncwarp();
+        wrote_smem = true;
       }
-      // S^T = K . Q^T over the 128 dims (two independent accumulation chains)
-      float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+      // S^T [64 t x 8 h] = K . Q^T: four token tiles, one accumulation chain each
+      float sacc[4][4];
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) sacc[mt][0] = sacc[mt][1] = sacc[mt][2] = sacc[mt][3] = 0.f;
       if (kFp8) {
-        // one ldmatrix.x4 = 16 tokens x 32 dims: chunk pair 2cc, 2cc+1
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
-          uint32_t x[4];
-          ldsm_x4(kbase + swz_off(0, k_row, 2 * cc + k_chunk8), x);
-          const uint32_t ka[4] = {f8lo(x[0]), f8lo(x[1]), f8hi(x[0]), f8hi(x[1])};
-          const uint32_t kb[4] = {f8lo(x[2]), f8lo(x[3]), f8hi(x[2]), f8hi(x[3])};
-          mma16816(s, ka, qb[2 * cc][0], qb[2 * cc][1]);
-          mma16816(s2, kb, qb[2 * cc + 1][0], qb[2 * cc + 1][1]);
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            uint32_t x[4];
+            ldsm_x4(kbase + koff[cc] + 2048 * mt, x);
+            const uint32_t ka[4] = {f8lo(x[0]), f8lo(x[1]), f8hi(x[0]), f8hi(x[1])};
+            const uint32_t kc[4] = {f8lo(x[2]), f8lo(x[3]), f8hi(x[2]), f8hi(x[3])};
+            mma16816(sacc[mt], ka, qb[2 * cc][0], qb[2 * cc][1]);
+            mma16816(sacc[mt], kc, qb[2 * cc + 1][0], qb[2 * cc + 1][1]);
+          }
         }
       } else {
 #pragma unroll
-      for (int ks = 0; ks < 8; ks += 2) {
-        uint32_t ka[4], kb[4];
-        const int dd = ks * 16 + k_dof;
-        ldsm_x4(kbase + swz_off(dd >> 6, k_row, (dd & 63) >> 3), ka);
-        ldsm_x4(kbase + swz_off((dd + 16) >> 6, k_row, ((dd + 16) & 63) >> 3), kb);
-        mma16816(s, ka, qb[ks][0], qb[ks][1]);
-        mma16816(s2, kb, qb[ks + 1][0], qb[ks + 1][1]);
+        for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+          for (int mt = 0; mt < 4; ++mt) {
+            uint32_t ka[4];
+            ldsm_x4(kbase + koff[ks] + 2048 * mt, ka);
+            mma16816(sacc[mt], ka, qb[ks][0], qb[ks][1]);
+          }
+        }
       }
+      // online softmax over the page's 64 tokens, heads hc and hc + 1
+      float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F;
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        const int t = mt * 16 + tr;
+        sacc[mt][0] = t < valid ? sacc[mt][0] * sc : -CUDART_INF_F;
+        sacc[mt][1] = t < valid ? sacc[mt][1] * sc : -CUDART_INF_F;
+        sacc[mt][2] = t + 8 < valid ? sacc[mt][2] * sc : -CUDART_INF_F;
+        sacc[mt][3] = t + 8 < valid ? sacc[mt][3] * sc : -CUDART_INF_F;
+        mx0 = fmaxf(mx0, fmaxf(sacc[mt][0], sacc[mt][2]));
+        mx1 = fmaxf(mx1, fmaxf(sacc[mt][1], sacc[mt][3]));
       }
-      // online softmax over this warp's 16 tokens, heads hc and hc + 1
-      const float x0 = tr < valid ? (s[0] + s2[0]) * sc : -CUDART_INF_F;
-      const float x1 = tr < valid ? (s[1] + s2[1]) * sc : -CUDART_INF_F;
-      const float x2 = tr + 8 < valid ? (s[2] + s2[2]) * sc : -CUDART_INF_F;
-      const float x3 = tr + 8 < valid ? (s[3] + s2[3]) * sc : -CUDART_INF_F;
-      const float mn0 = fmaxf(m0, quad_max(fmaxf(x0, x2)));
-      const float mn1 = fmaxf(m1, quad_max(fmaxf(x1, x3)));
-      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f, al0 = 1.f, al1 = 1.f;
-      if (mn0 != -CUDART_INF_F) {
-        p0 = exp2f(x0 - mn0);
-        p2 = exp2f(x2 - mn0);
-        al0 = exp2f(m0 - mn0);
+      const float mn0 = fmaxf(m0, quad_max(mx0));
+      const float mn1 = fmaxf(m1, quad_max(mx1));
+      const float e0 = mn0 == -CUDART_INF_F ? 0.f : mn0;  // exp2(-inf - 0) = 0 for an all-masked head
+      const float e1 = mn1 == -CUDART_INF_F ? 0.f : mn1;
+      const float al0 = exp2f(m0 - e0), al1 = exp2f(m1 - e1);
+      float ps0 = 0.f, ps1 = 0.f;
+      uint32_t pfr[4][2];  // P^T fragments of the four token tiles
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        const float p0 = exp2f(sacc[mt][0] - e0), p1 = exp2f(sacc[mt][1] - e1);
+        const float p2 = exp2f(sacc[mt][2] - e0), p3 = exp2f(sacc[mt][3] - e1);
+        ps0 += p0 + p2;
+        ps1 += p1 + p3;
+        pfr[mt][0] = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the tile
+        pfr[mt][1] = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
       }
-      if (mn1 != -CUDART_INF_F) {
-        p1 = exp2f(x1 - mn1);
-        p3 = exp2f(x3 - mn1);
-        al1 = exp2f(m1 - mn1);
-      }
-      l0 = l0 * al0 + quad_sum(p0 + p2);
-      l1 = l1 * al1 + quad_sum(p1 + p3);
+      l0 = l0 * al0 + quad_sum(ps0);
+      l1 = l1 * al1 + quad_sum(ps1);
       m0 = mn0;
       m1 = mn1;
 #pragma unroll
@@ -546,34 +575,37 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         o[mt][2] *= al0;
         o[mt][3] *= al1;
       }
-      const uint32_t pb0 = movmatrix_trans(pack_half2(p0, p1));  // tokens 0-7 of the warp
-      const uint32_t pb1 = movmatrix_trans(pack_half2(p2, p3));  // tokens 8-15
-      // O^T += V^T . P^T, 8 tiles of 16 dims
+      // O^T [128 d x 8 h] += V^T . P^T: eight dim tiles, four token steps each
       if (kFp8) {
-        // ldmatrix.trans (b16 view) of tokens 0-7 / 8-15 x chunk pair 2cc, 2cc+1;
+        // ldmatrix.trans (b16 view) of a token tile x chunk pair 2cc, 2cc+1;
         // byte permute {t2j d2i, t2j d2i+1, t2j+1 d2i, t2j+1 d2i+1} ->
         // {d2i: t2j, t2j+1 | d2i+1: t2j, t2j+1}
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t x[4];
-          ldsm_x4_t(vbase + swz_off(0, k_row, 2 * cc + k_chunk8), x);
+        for (int kt = 0; kt < 4; ++kt) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) x[i] = __byte_perm(x[i], 0u, 0x3120);
-          const uint32_t va[4] = {f8lo(x[0]), f8hi(x[0]), f8lo(x[1]), f8hi(x[1])};
-          const uint32_t vb[4] = {f8lo(x[2]), f8hi(x[2]), f8lo(x[3]), f8hi(x[3])};
-          mma16816(o[2 * cc], va, pb0, pb1);
-          mma16816(o[2 * cc + 1], vb, pb0, pb1);
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t x[4];
+            ldsm_x4_t(vbase + voff[cc] + 2048 * kt, x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = __byte_perm(x[i], 0u, 0x3120);
+            const uint32_t va[4] = {f8lo(x[0]), f8hi(x[0]), f8lo(x[1]), f8hi(x[1])};
+            const uint32_t vc[4] = {f8lo(x[2]), f8hi(x[2]), f8lo(x[3]), f8hi(x[3])};
+            mma16816(o[2 * cc], va, pfr[kt][0], pfr[kt][1]);
+            mma16816(o[2 * cc + 1], vc, pfr[kt][0], pfr[kt][1]);
+          }
         }
       } else {
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int dd = mt * 16 + v_dof;
-        uint32_t va[4];
-        ldsm_x4_t(vbase + swz_off(dd >> 6, v_row, (dd & 63) >> 3), va);
-        mma16816(o[mt], va, pb0, pb1);
+        for (int kt = 0; kt < 4; ++kt) {
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            uint32_t va[4];
+            ldsm_x4_t(vbase + voff[mt] + 2048 * kt, va);
+            mma16816(o[mt], va, pfr[kt][0], pfr[kt][1]);
+          }
+        }
       }
-      }
-      if (partial || wrote_smem) fence_proxy_async_smem();  // st.shared before the next TMA write
+      if (wrote_smem) fence_proxy_async_smem();  // st.shared before the next TMA write
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);

@@ -25,7 +25,8 @@ __device__ __forceinline__ __half2 fp8_inv_scale2(__half scale) {
 // Two fp16 (packed in x, element 0 in the low half) -> two e4m3 (element 0 in
 // the low byte).  NaN propagates through the clamp as in torch.clamp.
 __device__ __forceinline__ uint32_t quantize2_e4m3(uint32_t x, __half2 inv2) {
-  __half2 h = *reinterpret_cast<const __half2 *>(&x);
+  __half2 h = __halves2half2(__ushort_as_half(static_cast<unsigned short>(x & 0xffffu)),
+                             __ushort_as_half(static_cast<unsigned short>(x >> 16)));
   h = __hmul2(h, inv2);
   h = __hmin2_nan(__hmax2_nan(h, __float2half2_rn(-kFp8E4M3Max)), __float2half2_rn(kFp8E4M3Max));
   const __half2_raw r = h;
@@ -39,22 +40,28 @@ __device__ __forceinline__ uint2 quantize8_e4m3(uint4 v, __half2 inv2) {
 }
 
 // Two e4m3 (byte 0 in the low 8 bits of x) -> fp16x2 bits (element 0 in the
-// low half).  Exact: every e4m3 value is an fp16 value.
+// low half), by the hardware conversion.  Exact: every e4m3 value is an fp16
+// value.
 __device__ __forceinline__ uint32_t e4m3x2_to_half2(uint32_t x) {
-  const __half2_raw r = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(x & 0xffffu), __NV_E4M3);
-  return static_cast<uint32_t>(r.x) | (static_cast<uint32_t>(r.y) << 16);
+  uint32_t r;
+  const unsigned short pair = static_cast<unsigned short>(x & 0xffffu);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(pair));
+  return r;
+}
+
+// fp16x2 bits times an fp16x2 scale, as bits.
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t x, __half2 s) {
+  const __half2 h = __hmul2(__halves2half2(__ushort_as_half(static_cast<unsigned short>(x & 0xffffu)),
+                                           __ushort_as_half(static_cast<unsigned short>(x >> 16))),
+                            s);
+  return static_cast<uint32_t>(__half_as_ushort(__low2half(h))) |
+         (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16);
 }
 
 // Eight e4m3 -> eight fp16 times an fp16 scale.
 __device__ __forceinline__ uint4 dequantize8_e4m3(uint2 v, __half2 scale2) {
-  uint32_t w[4] = {e4m3x2_to_half2(v.x), e4m3x2_to_half2(v.x >> 16), e4m3x2_to_half2(v.y),
-                   e4m3x2_to_half2(v.y >> 16)};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __half2 h = __hmul2(*reinterpret_cast<const __half2 *>(&w[i]), scale2);
-    w[i] = *reinterpret_cast<const uint32_t *>(&h);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  return make_uint4(hmul2_bits(e4m3x2_to_half2(v.x), scale2), hmul2_bits(e4m3x2_to_half2(v.x >> 16), scale2),
+                    hmul2_bits(e4m3x2_to_half2(v.y), scale2), hmul2_bits(e4m3x2_to_half2(v.y >> 16), scale2));
 }
 
 }  // namespace b200kv

@@ -50,8 +50,7 @@ __global__ void __launch_bounds__(256) fp8_convert_kernel(const void *__restrict
           static_cast<uint8_t>(quantize2_e4m3(x, fp8_inv_scale2(s)) & 0xffu);
     } else {
       const uint32_t h = e4m3x2_to_half2(reinterpret_cast<const uint8_t *>(src)[i]);
-      const __half y = __hmul(*reinterpret_cast<const __half *>(&h), s);
-      reinterpret_cast<__half *>(dst)[i] = y;
+      reinterpret_cast<__half *>(dst)[i] = __hmul(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)), s);
     }
   }
 }
