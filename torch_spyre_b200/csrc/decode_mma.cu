@@ -53,6 +53,7 @@ namespace b200kv {
 namespace {
 
 constexpr int kConsumerWarps = 4;
+
 constexpr int kProducerWarp = kConsumerWarps;      // warp 4
 constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warp 5
 constexpr int kMmaThreads = (kConsumerWarps + 2) * 32;
@@ -122,9 +123,6 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
-// e4m3 pair (bytes 0, 1 of x) -> fp16x2 for an MMA fragment register
-__device__ __forceinline__ uint32_t f8lo(uint32_t x) { return e4m3x2_to_half2(x); }
-__device__ __forceinline__ uint32_t f8hi(uint32_t x) { return e4m3x2_to_half2(x >> 16); }
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t *>(&h);
@@ -517,10 +515,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         for (int cc = 0; cc < 4; ++cc) {
 #pragma unroll
           for (int mt = 0; mt < 4; ++mt) {
-            uint32_t x[4];
+            uint32_t x[4], ka[4], kc[4];
             ldsm_x4(kbase + koff[cc] + 2048 * mt, x);
-            const uint32_t ka[4] = {f8lo(x[0]), f8lo(x[1]), f8hi(x[0]), f8hi(x[1])};
-            const uint32_t kc[4] = {f8lo(x[2]), f8lo(x[3]), f8hi(x[2]), f8hi(x[3])};
+            // {dims 4j, 4j+1 | 4j+2, 4j+3} of rows r (x0, x2) and r + 8 (x1, x3)
+            e4m3x4_to_half2x2(x[0], ka[0], ka[2]);
+            e4m3x4_to_half2x2(x[1], ka[1], ka[3]);
+            e4m3x4_to_half2x2(x[2], kc[0], kc[2]);
+            e4m3x4_to_half2x2(x[3], kc[1], kc[3]);
             mma16816(sacc[mt], ka, qb[2 * cc][0], qb[2 * cc][1]);
             mma16816(sacc[mt], kc, qb[2 * cc + 1][0], qb[2 * cc + 1][1]);
           }
@@ -584,12 +585,14 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         for (int kt = 0; kt < 4; ++kt) {
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            uint32_t x[4];
+            uint32_t x[4], va[4], vc[4];
             ldsm_x4_t(vbase + voff[cc] + 2048 * kt, x);
 #pragma unroll
             for (int i = 0; i < 4; ++i) x[i] = __byte_perm(x[i], 0u, 0x3120);
-            const uint32_t va[4] = {f8lo(x[0]), f8hi(x[0]), f8lo(x[1]), f8hi(x[1])};
-            const uint32_t vc[4] = {f8lo(x[2]), f8hi(x[2]), f8lo(x[3]), f8hi(x[3])};
+            e4m3x4_to_half2x2(x[0], va[0], va[1]);
+            e4m3x4_to_half2x2(x[1], va[2], va[3]);
+            e4m3x4_to_half2x2(x[2], vc[0], vc[1]);
+            e4m3x4_to_half2x2(x[3], vc[2], vc[3]);
             mma16816(o[2 * cc], va, pfr[kt][0], pfr[kt][1]);
             mma16816(o[2 * cc + 1], vc, pfr[kt][0], pfr[kt][1]);
           }

@@ -49,6 +49,15 @@ __device__ __forceinline__ uint32_t e4m3x2_to_half2(uint32_t x) {
   return r;
 }
 
+// Four e4m3 (bytes 0..3 of x) -> fp16x2 of bytes 0, 1 (lo) and 2, 3 (hi), by
+// two hardware conversions on the halves of x.
+__device__ __forceinline__ void e4m3x4_to_half2x2(uint32_t x, uint32_t &lo, uint32_t &hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(x));
+}
+
 // fp16x2 bits times an fp16x2 scale, as bits.
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t x, __half2 s) {
   const __half2 h = __hmul2(__halves2half2(__ushort_as_half(static_cast<unsigned short>(x & 0xffffu)),
