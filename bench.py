@@ -64,6 +64,8 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--kv-dtype", default="fp16", choices=["fp16", "fp8"],
                    help="KV page element type: fp16 (the reference's) or e4m3 pages with per-pool fp16 scales")
+    p.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                   help="tp70b at N > 1: the o_proj all-reduce as libb200kv's peer-memory kernel or NCCL")
     p.add_argument("--nccl-graph", action="store_true",
                    help="tp70b at N > 1: capture the step, NCCL all-reduce included, in a CUDA graph")
     return p.parse_args()
@@ -255,11 +257,17 @@ def run_ours(args, rank, world, local):
         w_o = (torch.randn((hidden, len(shard.q_heads) * cfg.head_dim), generator=g, device=device,
                            dtype=torch.float16) * 0.02)
         partial = torch.empty((B, hidden), dtype=torch.float16, device=device)
+    ar = None
+    if tp and world > 1 and args.allreduce == "peer":
+        from torch_spyre_b200.tp import PeerAllReduce
+
+        ar = PeerAllReduce(B * cfg.hidden, device=device)
 
     def step(s):
         if tp:
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
-                                  out=partial, k_scale=s.k_scale, v_scale=s.v_scale)
+                                  out=partial if ar is None else None, k_scale=s.k_scale, v_scale=s.v_scale,
+                                  allreduce=ar)
         return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
                                     v_scale=s.v_scale)
 
@@ -279,7 +287,7 @@ def run_ours(args, rank, world, local):
     # Steps replay from CUDA graphs: one graph holding one step per rotating
     # input set (so consecutive steps run back to back without a graph launch
     # in between) plus one single-step graph per set for a remainder.
-    graphed = not (tp and world > 1) or args.nccl_graph
+    graphed = not (tp and world > 1) or args.nccl_graph or ar is not None
     with torch.cuda.stream(stream):
         for s in sets:  # warm the op once per set before capture
             step(s)
@@ -362,7 +370,7 @@ def run_ours(args, rank, world, local):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o)
+        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar)
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline_seconds > 0:
@@ -382,21 +390,28 @@ def run_ours(args, rank, world, local):
                    "global_batch": tokens_per_step, "num_q_heads": cfg.num_q_heads,
                    "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
                    "kv_heads_per_rank": sets[0].k_pool.shape[1], "kv_dtype": args.kv_dtype,
-                   "parallelism": (f"tp{world} (kv-head shards + NCCL all-reduce)" if tp else f"dp{world} (sequence shards)"),
+                   "parallelism": (f"tp{world} (kv-head shards + "
+                                   f"{'peer-memory' if ar is not None else 'NCCL'} all-reduce)" if tp
+                                   else f"dp{world} (sequence shards)"),
                    "l2": f"{n_sets} rotating input sets, {kv_bytes / 1e6:.1f} MB KV read per step (L2 126 MB)",
                    "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")},
         "kv_gbs": round(kv_bytes / (ms_per_step / 1e3) / 1e9, 1),
         "roofline": roofline,
         "e2e": e2e,
-        "gpu_launches": steps,  # one decode kernel per step (o_proj / all-reduce are cuBLAS / NCCL)
+        # one decode kernel per step, plus the peer all-reduce kernel at tp N > 1
+        # (o_proj is cuBLAS; an NCCL all-reduce is NCCL's)
+        "gpu_launches": steps * (2 if ar is not None else 1),
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if ar is not None:
+        del step_multi, step_single
+        ar.close()
 
 
-def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
+def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None):
     """Public-API decode step with host buffers: H2D inputs, append, decode, D2H.
 
     Each step's inputs (q, the new token's K/V rows, its slots, the block table
@@ -456,7 +471,7 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
             shard = HeadShard(int(os.environ.get("RANK", "0")), world, cfg.num_q_heads, cfg.num_kv_heads,
                               cfg.head_dim)
             o = tp_decode_step(shard, v["q"], s.k_pool, s.v_pool, v["block_table"], v["context_lens"], w_o,
-                               k_scale=s.k_scale, v_scale=s.v_scale)
+                               k_scale=s.k_scale, v_scale=s.v_scale, allreduce=ar)
         else:  # one launch: append the new token's K/V rows and decode
             o = tsb.decode_attention_append(v["q"], v["k_new"], v["v_new"], s.k_pool, s.v_pool,
                                             v["block_table"], v["context_lens"], k_scale=s.k_scale,
@@ -484,7 +499,7 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o):
 
     eager_ms = timed(eager_round)
     graph_ms = None
-    if not (tp and world > 1):
+    if not (tp and world > 1) or ar is not None:
         # the same public-API steps captured once and replayed: every replay
         # performs, per step, the host->device copy, the append, the decode
         # and the device->host copy of that step

@@ -310,6 +310,51 @@ B200KV_API int b200kv_decode_attention_append_fp8(
     void *workspace, int64_t workspace_bytes, int32_t *error_flag,
     void *stream);
 
+/* ------------------------------------------------------------------------ *
+ * Tensor-parallel all-reduce over peer memory.
+ *
+ * Replaces the o_proj all-reduce of the head-sharded decode step: the
+ * reference's TP collective is a SUM all-reduce of one tensor
+ * (SpyreCCLBackend::allreduce, torch_spyre/csrc/distributed/
+ * spyre_ccl.cpp:470-494).  Each rank (one process per GPU) allocates a peer
+ * buffer, exports it with b200kv_ipc_get_handle, exchanges the handle bytes
+ * with the other ranks by any host channel, maps theirs with
+ * b200kv_ipc_open_handle, and passes the table of all ranks' buffers (own
+ * included, in rank order) to b200kv_peer_allreduce_f16.  The tensor is the
+ * first num_elems fp16 of the rank's buffer (its "data" region, at offset
+ * 0): the rank's partial on entry, the elementwise sum over ranks on exit
+ * (fp32 accumulation in rank order, rounded to fp16 once; bit-identical on
+ * every rank).  Data moves with peer stores over NVLink; no multicast.
+ * Every rank must make the same calls (same num_elems, capacity and ctas) in
+ * the same order, like a collective; a call waits for its peers at most 2 s
+ * (then B200KV_DEVERR_TIMEOUT is OR-ed into error_flag and the result is
+ * undefined).  Calls replay correctly from CUDA graphs.
+ * ------------------------------------------------------------------------ */
+
+/* Bytes of one peer buffer for tensors of up to capacity_elems fp16 over
+ * world ranks (-1 on bad arguments). */
+B200KV_API int64_t b200kv_peer_buffer_bytes(int64_t capacity_elems, int32_t world);
+
+/* Allocates (cudaMalloc) and zeroes a peer buffer on the current device. */
+B200KV_API int b200kv_peer_alloc(int64_t capacity_elems, int32_t world, void **buffer_out);
+B200KV_API int b200kv_peer_free(void *buffer);
+
+/* CUDA IPC handle of a buffer (b200kv_ipc_handle_bytes() bytes) and the
+ * mapping of a peer's buffer into this process. */
+B200KV_API int32_t b200kv_ipc_handle_bytes(void);
+B200KV_API int b200kv_ipc_get_handle(void *buffer, void *handle_out);
+B200KV_API int b200kv_ipc_open_handle(const void *handle, void **buffer_out);
+B200KV_API int b200kv_ipc_close_handle(void *buffer);
+
+/* In-place SUM all-reduce of the first num_elems fp16 of every rank's buffer.
+ * peer_buffers: host array of world device pointers (rank order).
+ * num_elems and capacity_elems: multiples of 8 * world; ctas: CTAs per rank
+ * (0 = 32, at most 64). */
+B200KV_API int b200kv_peer_allreduce_f16(void *const *peer_buffers, int32_t rank,
+                                         int32_t world, int64_t num_elems,
+                                         int64_t capacity_elems, int32_t ctas,
+                                         int32_t *error_flag, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -88,3 +88,22 @@ def test_append_and_relayout_checks():
 def test_error_raises_runtime_error():
     with pytest.raises(RuntimeError, match="B200KV_ERR_INVALID_ARG"):
         _lib.call("b200kv_relayout_f16", 16, 16, 16, 64, 8, 128, 4, 5, None, None)
+
+
+def test_peer_allreduce_host_checks():
+    import ctypes
+
+    lib = _lib.lib()
+    assert lib.b200kv_ipc_handle_bytes() == 64
+    assert lib.b200kv_peer_buffer_bytes(128 * 8192, 2) > 128 * 8192 * 2 * 2
+    assert lib.b200kv_peer_buffer_bytes(0, 2) == -1 and lib.b200kv_peer_buffer_bytes(16, 9) == -1
+    table = (ctypes.c_void_p * 2)(1 << 20, 1 << 21)
+    assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 12, 32, 0, None, None) == 1
+    assert "multiple of 8 * world" in _lib.last_error()
+    assert lib.b200kv_peer_allreduce_f16(table, 2, 2, 16, 32, 0, None, None) == 1
+    assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 16, 32, 65, None, None) == 1
+    assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 48, 32, 0, None, None) == 1  # beyond capacity
+    assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 0, 32, 0, None, None) == 0  # nothing to do
+    bad = (ctypes.c_void_p * 2)(1 << 20, (1 << 21) + 16)
+    assert lib.b200kv_peer_allreduce_f16(bad, 0, 2, 16, 32, 0, None, None) == 1
+    assert "aligned" in _lib.last_error()

@@ -28,6 +28,7 @@ SOURCES = [
     "decode_noalloc.cu",
     "stick_relayout.cu",
     "fp8_ops.cu",
+    "peer_allreduce.cu",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -10,16 +10,22 @@ columns of the output projection W_o.  A step is
 
 The all-reduce is the reference's tensor-parallel collective: a synchronous
 SUM all-reduce of one tensor (SpyreCCLBackend::allreduce,
-torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494), here over NCCL on
-NVLink/NVSwitch.  The block table and context lengths are replicated.
+torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494).  It runs either over NCCL
+on NVLink/NVSwitch or, with a :class:`PeerAllReduce`, as one libb200kv kernel
+per rank over buffers the ranks map into each other with CUDA IPC (two-shot:
+push slices to their owner, owner sums and pushes the result to every rank).
+The block table and context lengths are replicated.
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
+
+from . import _lib
 
 
 @dataclass(frozen=True)
@@ -72,6 +78,96 @@ class HeadShard:
         return w_o[:, self.w_cols].contiguous()
 
 
+class _DeviceBytes:
+    """A raw device allocation seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 2, "strides": None}
+
+
+class PeerAllReduce:
+    """SUM all-reduce of fp16 tensors of up to ``capacity`` elements over peer
+    memory (libb200kv ``b200kv_peer_allreduce_f16``).
+
+    Every rank allocates one peer buffer, exports its CUDA IPC handle and maps
+    the others' (exchanged with ``all_gather_object`` over ``group``).  The
+    tensor to reduce lives in the buffer's data region: ``buffer(shape)`` is a
+    view a producer writes (the o_proj GEMM), ``all_reduce(view)`` sums it in
+    place across ranks on the current stream.  Every rank must call
+    ``all_reduce`` the same number of times with the same sizes, like a
+    collective; calls replay correctly from CUDA graphs.  Waits are bounded:
+    a missing peer sets B200KV_DEVERR_TIMEOUT in ``error_flag`` after 2 s.
+    """
+
+    def __init__(self, capacity: int, group=None, device: Optional[torch.device] = None, ctas: int = 32):
+        import torch.distributed as dist
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        q = 8 * self.world
+        self.capacity = -(-int(capacity) // q) * q
+        self.ctas = int(ctas)
+        lib = _lib.lib()
+        with torch.cuda.device(self.device):
+            buf = ctypes.c_void_p()
+            _lib.call("b200kv_peer_alloc", self.capacity, self.world, ctypes.byref(buf))
+            self._own = buf.value
+            hbytes = lib.b200kv_ipc_handle_bytes()
+            handle = (ctypes.c_char * hbytes)()
+            _lib.call("b200kv_ipc_get_handle", ctypes.c_void_p(self._own), handle)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._opened = []
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.call("b200kv_ipc_open_handle", ctypes.create_string_buffer(h, len(h)), ctypes.byref(p))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+        self._table = (ctypes.c_void_p * self.world)(*ptrs)
+        self._data = torch.as_tensor(_DeviceBytes(self._own, self.capacity * 2), device=self.device).view(torch.float16)
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def buffer(self, shape) -> torch.Tensor:
+        """A view of the data region (fp16, contiguous) of the given shape."""
+        n = 1
+        for d in shape:
+            n *= int(d)
+        if n > self.capacity:
+            raise ValueError(f"{n} elements exceed the peer buffer capacity {self.capacity}")
+        return self._data[:n].view(*shape)
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        """Sums ``t`` (a view from ``buffer``) over the ranks, in place."""
+        if t.dtype != torch.float16 or not t.is_contiguous() or t.data_ptr() != self._data.data_ptr():
+            raise ValueError("all_reduce takes a contiguous fp16 view returned by buffer()")
+        _lib.call("b200kv_peer_allreduce_f16", self._table, self.rank, self.world, t.numel(), self.capacity,
+                  self.ctas, self.error_flag.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        return t
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (after a barrier:
+        no peer may still write into it)."""
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._data = None
+        for p in self._opened:
+            _lib.call("b200kv_ipc_close_handle", ctypes.c_void_p(p))
+        _lib.call("b200kv_peer_free", ctypes.c_void_p(self._own))
+        self._own = None
+        self._opened = []
+
+
 AttnFn = Callable[..., torch.Tensor]
 
 
@@ -88,11 +184,15 @@ def tp_decode_step(
     attn_fn: Optional[AttnFn] = None,
     k_scale: Optional[torch.Tensor] = None,
     v_scale: Optional[torch.Tensor] = None,
+    allreduce: Optional[PeerAllReduce] = None,
 ) -> torch.Tensor:
     """One rank's step: local decode -> o_proj partial -> SUM all-reduce.
 
     attn_fn defaults to the CUDA decode op; tests on CPU ranks pass the oracle.
-    k_scale / v_scale are the dequantisation scales of fp8 pools.
+    k_scale / v_scale are the dequantisation scales of fp8 pools.  With
+    ``allreduce`` the partial is written into its peer buffer and reduced by
+    the peer-memory kernel (the result is a view of that buffer, valid until
+    the next step); otherwise NCCL (``group``) reduces it.
     Every rank must call this in the same order (it contains one collective).
     """
     if attn_fn is None:
@@ -103,6 +203,10 @@ def tp_decode_step(
         attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens)
     B = attn.shape[0]
     flat = attn.reshape(B, -1)
+    if allreduce is not None:
+        partial = allreduce.buffer((B, w_o_local.shape[0]))
+        torch.matmul(flat, w_o_local.t(), out=partial)
+        return allreduce.all_reduce(partial)
     if out is not None:
         partial = torch.matmul(flat, w_o_local.t(), out=out)
     else:
