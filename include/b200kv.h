@@ -349,7 +349,7 @@ B200KV_API int b200kv_ipc_close_handle(void *buffer);
 /* In-place SUM all-reduce of the first num_elems fp16 of every rank's buffer.
  * peer_buffers: host array of world device pointers (rank order).
  * num_elems and capacity_elems: multiples of 8 * world; ctas: CTAs per rank
- * (0 = 32, at most 64). */
+ * (0 = 128, at most 128). */
 B200KV_API int b200kv_peer_allreduce_f16(void *const *peer_buffers, int32_t rank,
                                          int32_t world, int64_t num_elems,
                                          int64_t capacity_elems, int32_t ctas,

@@ -101,7 +101,7 @@ def test_peer_allreduce_host_checks():
     assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 12, 32, 0, None, None) == 1
     assert "multiple of 8 * world" in _lib.last_error()
     assert lib.b200kv_peer_allreduce_f16(table, 2, 2, 16, 32, 0, None, None) == 1
-    assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 16, 32, 65, None, None) == 1
+    assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 16, 32, 129, None, None) == 1
     assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 48, 32, 0, None, None) == 1  # beyond capacity
     assert lib.b200kv_peer_allreduce_f16(table, 0, 2, 0, 32, 0, None, None) == 0  # nothing to do
     bad = (ctypes.c_void_p * 2)(1 << 20, (1 << 21) + 16)

@@ -100,7 +100,7 @@ class PeerAllReduce:
     a missing peer sets B200KV_DEVERR_TIMEOUT in ``error_flag`` after 2 s.
     """
 
-    def __init__(self, capacity: int, group=None, device: Optional[torch.device] = None, ctas: int = 32):
+    def __init__(self, capacity: int, group=None, device: Optional[torch.device] = None, ctas: int = 128):
         import torch.distributed as dist
 
         self.group = group
