@@ -311,6 +311,56 @@ B200KV_API int b200kv_decode_attention_append_fp8(
     void *stream);
 
 /* ------------------------------------------------------------------------ *
+ * Rotary position embedding (RoPE) with the reference's formulation (the
+ * rope dataflow of tests/inductor/test_inductor_ops.py:5447-5456): a head row
+ * x of D elements is two halves x_0 = x[0 : D/2], x_1 = x[D/2 : D] and
+ *     out[i * D/2 + j] = sum_k freqs[pos][i][k][j] * x_k[j]    (i, k in {0, 1})
+ * with freqs fp16 [max_pos][2][2][D/2] (a 2x2 matrix per position and
+ * frequency); each product is rounded to fp16, the two products are summed
+ * in fp32 and the sum is rounded to fp16 (bit-exact with the reference's CPU
+ * path).  A position outside [0, max_pos) is clamped and sets
+ * B200KV_DEVERR_BAD_LEN.
+ * ------------------------------------------------------------------------ */
+
+/* Rotates rows x[t * x_stride_t + h * x_stride_h + d] (fp16, t < num_tokens,
+ * h < num_heads, d < head_dim) at positions[t] (int32) into out (may equal x).
+ * head_dim a multiple of 4; x, out and freqs 4-byte aligned, even strides. */
+B200KV_API int b200kv_rope_f16(const void *x, int64_t x_stride_t, int64_t x_stride_h,
+                               void *out, int64_t out_stride_t, int64_t out_stride_h,
+                               const void *freqs, int64_t max_pos,
+                               const int32_t *positions, int64_t num_tokens,
+                               int64_t num_heads, int64_t head_dim,
+                               int32_t *error_flag, void *stream);
+
+/* Fused append + decode with RoPE: as b200kv_decode_attention_append_f16 /
+ * _fp8, with q and the new K row rotated at position context_lens[b] - 1
+ * (rope_freqs fp16 [rope_max_pos][2][2][64]) before the K row is written and
+ * attention is computed.  Equals b200kv_rope_f16 on q and k_new followed by
+ * the plain fused call. */
+B200KV_API int b200kv_decode_attention_append_rope_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new,
+    const void *v_new, int64_t new_stride_b, int64_t new_stride_h, void *k_pool,
+    void *v_pool, const void *rope_freqs, int64_t rope_max_pos,
+    const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream);
+B200KV_API int b200kv_decode_attention_append_rope_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new,
+    const void *v_new, int64_t new_stride_b, int64_t new_stride_h, void *k_pool,
+    void *v_pool, const void *k_scale, const void *v_scale, const void *rope_freqs,
+    int64_t rope_max_pos, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    void *stream);
+
+/* ------------------------------------------------------------------------ *
  * Tensor-parallel all-reduce over peer memory.
  *
  * Replaces the o_proj all-reduce of the head-sharded decode step: the

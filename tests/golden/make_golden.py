@@ -16,7 +16,13 @@ hand SDPA [B, S, H, D] tensors without the transpose(1, 2) its prefill sets
 apply (and mark the cases expect_fail); the fixtures apply the transpose, so
 q is [B, H, 1, D] and k/v are [B, Hkv, 257, D].
 
-Writes sdpa_decode_golden.npz and index_copy_golden.json.
+The rotary embedding fixtures evaluate the reference's rope dataflow
+(tests/inductor/test_inductor_ops.py:5447-5456: view the row as two halves,
+multiply by freqs broadcast over the output half, sum over the input half,
+flatten) on its own param sets (2840-2858) with CPU fp16 tensors.
+
+Writes sdpa_decode_golden.npz, index_copy_golden.json and rope_golden.json /
+rope_golden.npz.
 """
 
 from __future__ import annotations
@@ -97,6 +103,24 @@ def main():
         "sha_after_decode": sha(after_decode),
     }
     (HERE / "index_copy_golden.json").write_text(json.dumps(ic, indent=1) + "\n")
+
+    # rotary embedding (test_inductor_ops.py:2840-2858 inputs, 5447-5456 dataflow)
+    rope_meta, rope_arrays = {"pinned_by_reference_cached_randn": pinned_by_reference}, {}
+    for name, qshape, fshape in [("prefill_bs1", (1, 256, 4096), (1, 256, 2, 2, 64)),
+                                 ("prefill", (2, 256, 4096), (1, 256, 2, 2, 64)),
+                                 ("decode_bs1", (1, 1, 4096), (1, 1, 2, 2, 64)),
+                                 ("decode", (2, 1, 4096), (1, 1, 2, 2, 64))]:
+        q, freqs = randn(qshape), randn(fshape)
+        B, S, E = q.shape
+        D = freqs.shape[-1] * 2
+        halves = q.view(B, S, E // D, 2, D // 2).unsqueeze(-3)      # [B, S, H, 1, 2, D/2]
+        out = (freqs[:, :, None] * halves).sum(4, keepdim=True).flatten(3)
+        rope_meta[name] = {"q_shape": list(qshape), "freqs_shape": list(fshape), "sha_q": sha(q),
+                           "sha_freqs": sha(freqs), "sha_out": sha(out), "out_shape": list(out.shape)}
+        if S == 1:
+            rope_arrays[f"{name}_out"] = out.numpy()
+    (HERE / "rope_golden.json").write_text(json.dumps(rope_meta, indent=1) + "\n")
+    np.savez_compressed(HERE / "rope_golden.npz", **rope_arrays)
     (HERE / "sdpa_decode_golden.json").write_text(json.dumps(meta, indent=1) + "\n")
     print("wrote fixtures; pinned by reference cached_randn:", pinned_by_reference)
 

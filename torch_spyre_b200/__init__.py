@@ -10,7 +10,7 @@ from ._lib import B200KVError
 from .fp8 import dequantize_fp8_with_scale, empty_pool_fp8, pool_shape_fp8, quantize_fp8_with_scale
 from .layout import (SpyreTensorLayout, empty_pool, from_device_layout, page_layout, pool_shape, stick_layout,
                      to_device_layout)
-from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout,
+from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout, rope,
                   sdpa_decode)
 
 __all__ = [
@@ -30,6 +30,7 @@ __all__ = [
     "pool_shape",
     "pool_shape_fp8",
     "quantize_fp8_with_scale",
+    "rope",
     "sdpa_decode",
     "stick_layout",
 ]

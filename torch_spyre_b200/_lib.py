@@ -107,6 +107,43 @@ SIGNATURES = {
         ctypes.c_int,
         [_p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p, _p],
     ),
+    "b200kv_rope_f16": (ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p]),
+    "b200kv_decode_attention_append_rope_f16": (
+        ctypes.c_int,
+        [
+            _p, _i64, _i64,  # q, q_stride_b, q_stride_h
+            _p, _p, _i64, _i64,  # k_new, v_new, new_stride_b, new_stride_h
+            _p, _p,  # k_pool, v_pool
+            _p, _i64,  # rope_freqs, rope_max_pos
+            _p, _i64,  # block_table, block_table_stride
+            _p,  # context_lens
+            _p, _i64, _i64,  # out, out_stride_b, out_stride_h
+            _p,  # lse
+            _i64, _i64, _i64, _i64,  # batch, Hq, Hkv, head_dim
+            _i64, _i64,  # num_blocks, max_blocks_per_seq
+            _f32, _i64,  # scale, num_splits
+            _p, _i64,  # workspace, workspace_bytes
+            _p, _p,  # error_flag, stream
+        ],
+    ),
+    "b200kv_decode_attention_append_rope_fp8": (
+        ctypes.c_int,
+        [
+            _p, _i64, _i64,  # q, q_stride_b, q_stride_h
+            _p, _p, _i64, _i64,  # k_new, v_new, new_stride_b, new_stride_h
+            _p, _p, _p, _p,  # k_pool, v_pool, k_scale, v_scale
+            _p, _i64,  # rope_freqs, rope_max_pos
+            _p, _i64,  # block_table, block_table_stride
+            _p,  # context_lens
+            _p, _i64, _i64,  # out, out_stride_b, out_stride_h
+            _p,  # lse
+            _i64, _i64, _i64, _i64,  # batch, Hq, Hkv, head_dim
+            _i64, _i64,  # num_blocks, max_blocks_per_seq
+            _f32, _i64,  # scale, num_splits
+            _p, _i64,  # workspace, workspace_bytes
+            _p, _p,  # error_flag, stream
+        ],
+    ),
     "b200kv_peer_buffer_bytes": (_i64, [_i64, _i32]),
     "b200kv_peer_alloc": (ctypes.c_int, [_i64, _i32, _p]),
     "b200kv_peer_free": (ctypes.c_int, [_p]),

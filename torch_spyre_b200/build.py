@@ -29,6 +29,7 @@ SOURCES = [
     "stick_relayout.cu",
     "fp8_ops.cu",
     "peer_allreduce.cu",
+    "rope.cu",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

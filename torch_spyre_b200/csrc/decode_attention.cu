@@ -53,7 +53,7 @@ static int decode_entry(
     float scale, int64_t num_splits, void *workspace, int64_t workspace_bytes,
     int32_t *error_flag, void *stream, const void *k_new, const void *v_new, int64_t new_sb,
     int64_t new_sh, bool append, bool fp8 = false, const void *k_scale = nullptr,
-    const void *v_scale = nullptr) {
+    const void *v_scale = nullptr, const void *rope_freqs = nullptr, int64_t rope_max_pos = 0) {
   clear_error();
   B200KV_CHECK_ARG(batch >= 0, "batch must be >= 0");
   B200KV_CHECK_ARG(num_q_heads > 0 && num_kv_heads > 0, "head counts must be > 0");
@@ -102,6 +102,11 @@ static int decode_entry(
     if (use_simt_kernel())
       return set_error(B200KV_ERR_UNSUPPORTED, "fused append needs the tensor-core kernel");
   }
+  if (rope_freqs) {
+    B200KV_CHECK_ARG(append, "the rotary embedding applies to the fused append only");
+    B200KV_CHECK_ARG(rope_max_pos > 0, "rope_max_pos must be > 0");
+    B200KV_CHECK_ARG((reinterpret_cast<uintptr_t>(rope_freqs) & 3u) == 0, "rope_freqs must be 4-byte aligned");
+  }
   if (fp8) {
     B200KV_CHECK_ARG(k_scale && v_scale, "k_scale / v_scale must not be null");
     if (use_simt_kernel())
@@ -143,6 +148,10 @@ static int decode_entry(
     a.new_sh = new_sh;
     a.k_pool_w = static_cast<__half *>(const_cast<void *>(k_pool));
     a.v_pool_w = static_cast<__half *>(const_cast<void *>(v_pool));
+  }
+  if (rope_freqs) {
+    a.rope_freqs = static_cast<const __half *>(rope_freqs);
+    a.rope_max_pos = rope_max_pos;
   }
   if (fp8) {
     a.k_scale = static_cast<const __half *>(k_scale);
@@ -219,4 +228,36 @@ extern "C" int b200kv_decode_attention_append_fp8(
                       num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
                       workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
                       new_stride_h, true, true, k_scale, v_scale);
+}
+
+extern "C" int b200kv_decode_attention_append_rope_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new, const void *v_new,
+    int64_t new_stride_b, int64_t new_stride_h, void *k_pool, void *v_pool, const void *rope_freqs,
+    int64_t rope_max_pos, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b, int64_t out_stride_h, float *lse,
+    int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits, void *workspace,
+    int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+  B200KV_CHECK_ARG(rope_freqs, "rope_freqs must not be null");
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
+                      new_stride_h, true, false, nullptr, nullptr, rope_freqs, rope_max_pos);
+}
+
+extern "C" int b200kv_decode_attention_append_rope_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new, const void *v_new,
+    int64_t new_stride_b, int64_t new_stride_h, void *k_pool, void *v_pool, const void *k_scale,
+    const void *v_scale, const void *rope_freqs, int64_t rope_max_pos, const int32_t *block_table,
+    int64_t block_table_stride, const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+  B200KV_CHECK_ARG(rope_freqs, "rope_freqs must not be null");
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
+                      new_stride_h, true, true, k_scale, v_scale, rope_freqs, rope_max_pos);
 }

@@ -46,6 +46,10 @@ struct DecodeArgs {
   // quantised new rows through k_pool8_w / v_pool8_w.
   const __half *k_scale = nullptr, *v_scale = nullptr;
   uint8_t *k_pool8_w = nullptr, *v_pool8_w = nullptr;
+  // Rotary embedding on append (null: none): q and the new K row are rotated
+  // with rope_freqs[context_len - 1] ([max_pos][2][2][64] fp16, rope.cuh).
+  const __half *rope_freqs = nullptr;
+  int64_t rope_max_pos = 0;
 };
 
 struct WorkspaceLayout {

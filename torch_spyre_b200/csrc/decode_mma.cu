@@ -33,6 +33,11 @@
 //             completion ticket and, holding the last one, merges the pair's
 //             partials (online log-sum-exp, decode_common.cuh).
 //
+// Fused append (kAppend) may also apply the rotary embedding (rope.cuh) of
+// position context_len - 1 to q and to the new K row: q in its MMA fragments
+// (dims j and j + 64 sit in the same lane, in steps ks and ks + 4), the K row
+// in the append path (16-byte chunks c and c ^ 8 meet by one shuffle).
+//
 // FP8 pages (kFp8): the pools hold e4m3 values, one 128-byte stick per token
 // row (8 KiB pages).  The consumers widen them to fp16 in registers (exact) and
 // run the same fp16 MMAs; because both contractions are sums, the order of
@@ -48,6 +53,7 @@
 // The K scale folds into the softmax scale, the V scale into the epilogue.
 #include "decode_kernels.h"
 #include "fp8.cuh"
+#include "rope.cuh"
 
 namespace b200kv {
 namespace {
@@ -423,6 +429,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   float o[8][4];
   float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
 
+  // Row of the rotary table for a sequence of `ctx` tokens (its new token at
+  // ctx - 1); out of range is flagged and clamped.
+  auto rope_pos = [&](int ctx) -> int64_t {
+    int64_t pos = int64_t(ctx) - 1;
+    if (pos < 0 || pos >= a.rope_max_pos) {
+      if (lane == 0 && a.error_flag) atomicOr(a.error_flag, B200KV_DEVERR_BAD_LEN);
+      pos = pos < 0 ? 0 : a.rope_max_pos - 1;
+    }
+    return pos;
+  };
+
   // The appended token's rows replace the staged ones (the page's warp writes
   // them into the stage's K/V pages and into the pools).
   auto apply_append = [&](int st, const StageDesc &dd) {
@@ -430,7 +447,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const int c = lane & 15;  // 16-byte chunk of the row; lanes 0-15 K, 16-31 V
     const int kv = lane >> 4;
     const uint8_t *src = smem + L::kNew + st * 2 * kHeadDim * 2 + kv * kHeadDim * 2 + c * 16;
-    const uint4 v = *reinterpret_cast<const uint4 *>(src);
+    uint4 v = *reinterpret_cast<const uint4 *>(src);
+    if (a.rope_freqs != nullptr) {  // rotate the K row: chunk c pairs with chunk c ^ 8
+      uint32_t w[4] = {v.x, v.y, v.z, v.w}, pw[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pw[i] = __shfl_xor_sync(0xffffffffu, w[i], 8);
+      if (kv == 0) {
+        const __half *f = a.rope_freqs + rope_pos(dd.ctx) * 4 * (kHeadDim / 2);
+        const bool lo = c < 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t x0 = lo ? w[i] : pw[i], x1 = lo ? pw[i] : w[i];
+          rope_pair(f, kHeadDim / 2, 8 * (c & 7) + 2 * i, x0, x1);
+          w[i] = lo ? x0 : x1;
+        }
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
     if (kFp8) {  // quantise: dims 8c..8c+7 are bytes 8c..8c+7 of the page row
       const uint2 q8 = quantize8_e4m3(v, kv ? vinv : kinv);
       *reinterpret_cast<uint2 *>(smem + st * L::kStageBytes + kv * L::kPage + swz_off(0, t_new, c >> 1) +
@@ -485,6 +518,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           }
           qb[ks][0] = x0;
           qb[ks][1] = x1;
+        }
+        if (kAppend && a.rope_freqs != nullptr) {  // rotate q: dims e and e + 64 are steps ks, ks + 4
+          const __half *f = a.rope_freqs + rope_pos(d.ctx) * 4 * (kHeadDim / 2);
+          if (qh < G) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const int e0 = kFp8 ? 16 * ks + 4 * (lane & 3) : 16 * ks + hc;
+              rope_pair(f, kHeadDim / 2, e0, qb[ks][0], qb[ks + 4][0]);
+              rope_pair(f, kHeadDim / 2, kFp8 ? e0 + 2 : e0 + 8, qb[ks][1], qb[ks + 4][1]);
+            }
+          }
         }
       }
     }

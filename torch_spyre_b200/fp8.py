@@ -24,7 +24,7 @@ import torch
 
 from . import _lib
 from .layout import PAGE_TOKENS
-from .ops import _maybe_check_flag, _ptr, _require_cuda, _stream_ptr, workspace_for
+from .ops import _check_rope_freqs, _maybe_check_flag, _ptr, _require_cuda, _stream_ptr, workspace_for
 
 FP8 = torch.float8_e4m3fn
 FP8_E4M3_MAX = 448.0
@@ -257,6 +257,7 @@ def _decode_attention_append_fp8_op(
     scale: float,
     num_splits: int,
     error_flag: Optional[torch.Tensor],
+    rope_freqs: Optional[torch.Tensor] = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     _require_cuda(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale, block_table, context_lens)
     _check_pool8(k_pool, "k_pool")
@@ -277,11 +278,12 @@ def _decode_attention_append_fp8_op(
         return out, lse
     wbytes = _lib.lib().b200kv_decode_workspace_bytes(B, Hq, Hkv, D)
     ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
+    rope = () if rope_freqs is None else (_check_rope_freqs(rope_freqs, D, q.device).data_ptr(), rope_freqs.shape[0])
     _lib.call(
-        "b200kv_decode_attention_append_fp8",
+        "b200kv_decode_attention_append_rope_fp8" if rope else "b200kv_decode_attention_append_fp8",
         q.data_ptr(), q.stride(0), q.stride(1),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
-        k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
+        k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), *rope,
         block_table.data_ptr(), block_table.stride(0),
         context_lens.data_ptr(),
         out.data_ptr(), out.stride(0), out.stride(1),
@@ -297,6 +299,6 @@ def _decode_attention_append_fp8_op(
 
 @_decode_attention_append_fp8_op.register_fake
 def _(q, k_new, v_new, k_pool, v_pool, k_scale, v_scale, block_table, context_lens, scale, num_splits,
-      error_flag):
+      error_flag, rope_freqs=None):
     B, Hq, D = q.shape
     return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)

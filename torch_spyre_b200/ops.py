@@ -15,6 +15,10 @@ Operator surface, mirroring the reference's hot-path ops:
 * ``b200kv::kv_append(k_new, v_new, k_pool!, v_pool!, slot_mapping)`` -- the
   KV slot write, in place like ``spyre::overwrite`` (customops.py:262-295,
   ``mutates_args``) and ``Tensor.index_copy_`` (ops/fallbacks.py:256).
+* ``b200kv::rope(x, freqs, positions) -> out`` -- the rotary embedding with the
+  reference's formulation (tests/inductor/test_inductor_ops.py:5447-5456);
+  ``decode_attention_append(..., rope_freqs=)`` applies it to q and the new K
+  row inside the fused kernel.
 * ``b200kv::kv_relayout(rows, pool!, block_ids)`` /
   ``b200kv::kv_unrelayout(pool, block_ids, num_tokens) -> rows`` -- the
   row-major <-> stick-page relayout (spyre_mem.cpp:176-440 as an HBM kernel).
@@ -212,6 +216,7 @@ def _decode_attention_append_op(
     scale: float,
     num_splits: int,
     error_flag: Optional[torch.Tensor],
+    rope_freqs: Optional[torch.Tensor] = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     _require_cuda(q, k_new, v_new, k_pool, v_pool, block_table, context_lens)
     if q.dim() != 3 or q.dtype != torch.float16 or q.stride(2) != 1:
@@ -234,11 +239,12 @@ def _decode_attention_append_op(
     lib = _lib.lib()
     wbytes = lib.b200kv_decode_workspace_bytes(B, Hq, Hkv, D)
     ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
+    rope = () if rope_freqs is None else (_check_rope_freqs(rope_freqs, D, q.device).data_ptr(), rope_freqs.shape[0])
     _lib.call(
-        "b200kv_decode_attention_append_f16",
+        "b200kv_decode_attention_append_rope_f16" if rope else "b200kv_decode_attention_append_f16",
         q.data_ptr(), q.stride(0), q.stride(1),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
-        k_pool.data_ptr(), v_pool.data_ptr(),
+        k_pool.data_ptr(), v_pool.data_ptr(), *rope,
         block_table.data_ptr(), block_table.stride(0),
         context_lens.data_ptr(),
         out.data_ptr(), out.stride(0), out.stride(1),
@@ -253,7 +259,7 @@ def _decode_attention_append_op(
 
 
 @_decode_attention_append_op.register_fake
-def _(q, k_new, v_new, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag):
+def _(q, k_new, v_new, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag, rope_freqs=None):
     B, Hq, D = q.shape
     return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)
 
@@ -272,6 +278,7 @@ def decode_attention_append(
     error_flag: Optional[torch.Tensor] = None,
     k_scale: Optional[torch.Tensor] = None,
     v_scale: Optional[torch.Tensor] = None,
+    rope_freqs: Optional[torch.Tensor] = None,
 ):
     """Appends the new token's K/V rows ([B, Hkv, D], at position
     context_lens[b] - 1) to the pools and decodes, in one launch.
@@ -279,20 +286,68 @@ def decode_attention_append(
     Same result as ``kv_append`` at those slots followed by
     ``decode_attention`` (the HF ``index_copy_`` + SDPA step of the reference).
     fp8 pools take ``k_scale`` / ``v_scale``; the new rows are quantized.
+    With ``rope_freqs`` ([max_pos, 2, 2, D/2] fp16, or the reference's
+    [1, max_pos, 2, 2, D/2]) q and the new K row are first rotated at position
+    context_lens[b] - 1, as ``rope`` would.
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
+    if rope_freqs is not None and rope_freqs.dim() == 5:
+        rope_freqs = rope_freqs[0]
     if _is_fp8(k_pool):
         from . import fp8  # noqa: F401
         out, lse = torch.ops.b200kv.decode_attention_append_fp8(
             q, k_new, v_new, k_pool, v_pool, _need(k_scale, "k_scale"), _need(v_scale, "v_scale"), block_table,
-            context_lens, float(scale), int(num_splits), error_flag
+            context_lens, float(scale), int(num_splits), error_flag, rope_freqs
         )
     else:
         out, lse = torch.ops.b200kv.decode_attention_append(
-            q, k_new, v_new, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
+            q, k_new, v_new, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag,
+            rope_freqs
         )
     return (out, lse) if return_lse else out
+
+
+# -------------------------------------------------------------------- rope --
+def _check_rope_freqs(freqs: torch.Tensor, head_dim: int, device: torch.device) -> torch.Tensor:
+    if freqs.dtype != torch.float16 or freqs.dim() != 4 or tuple(freqs.shape[1:]) != (2, 2, head_dim // 2):
+        raise ValueError(f"rope freqs must be fp16 [max_pos, 2, 2, {head_dim // 2}], got {tuple(freqs.shape)}")
+    if not freqs.is_contiguous() or freqs.device != device:
+        raise ValueError("rope freqs must be contiguous and on the device of the rows")
+    return freqs
+
+
+@torch.library.custom_op("b200kv::rope", mutates_args=(), device_types="cuda")
+def _rope_op(x: torch.Tensor, freqs: torch.Tensor, positions: torch.Tensor,
+             error_flag: Optional[torch.Tensor]) -> torch.Tensor:
+    _require_cuda(x, freqs, positions)
+    if x.dim() != 3 or x.dtype != torch.float16 or x.stride(2) != 1:
+        raise ValueError(f"x must be fp16 [T, H, D] with a contiguous head_dim, got {tuple(x.shape)}")
+    T, H, D = x.shape
+    _check_rope_freqs(freqs, D, x.device)
+    if positions.dtype != torch.int32 or positions.shape != (T,) or not positions.is_contiguous():
+        raise ValueError("positions must be a contiguous int32 [T] tensor")
+    out = torch.empty((T, H, D), dtype=torch.float16, device=x.device)
+    _lib.call("b200kv_rope_f16", x.data_ptr(), x.stride(0), x.stride(1), out.data_ptr(), out.stride(0),
+              out.stride(1), freqs.data_ptr(), freqs.shape[0], positions.data_ptr(), T, H, D, _ptr(error_flag),
+              _stream_ptr(x.device))
+    _maybe_check_flag(error_flag, "rope")
+    return out
+
+
+@_rope_op.register_fake
+def _(x, freqs, positions, error_flag):
+    return torch.empty_like(x)
+
+
+def rope(x: torch.Tensor, freqs: torch.Tensor, positions: torch.Tensor,
+         error_flag: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Rotary embedding of rows x [T, H, D] at positions [T] (int32) with
+    freqs [max_pos, 2, 2, D/2] (or the reference's [1, max_pos, 2, 2, D/2]):
+    out[..., i*D/2 + j] = sum_k freqs[pos, i, k, j] * x[..., k*D/2 + j]."""
+    if freqs.dim() == 5:
+        freqs = freqs[0]
+    return torch.ops.b200kv.rope(x, freqs, positions, error_flag)
 
 
 # ------------------------------------------------------------------ append --
