@@ -4,7 +4,8 @@
 // freqs[pos] is [2][2][D/2] (a 2x2 matrix per frequency j) and
 //     out[i * D/2 + j] = sum_k freqs[pos][i][k][j] * x_k[j]      (i, k in {0, 1})
 // computed as the reference's CPU path does it: each product rounded to fp16,
-// the two products summed in fp32, the sum rounded to fp16.
+// the two products summed in fp32 from a +0 accumulator, the sum rounded to
+// fp16.
 #pragma once
 
 #include "common.cuh"
@@ -26,8 +27,9 @@ __device__ __forceinline__ void rope_pair(const __half *__restrict__ f, int half
   const __half2 f11 = __ldg(reinterpret_cast<const __half2 *>(f + 3 * half_d + e));
   const float2 p00 = __half22float2(__hmul2(f00, a)), p01 = __half22float2(__hmul2(f01, b));
   const float2 p10 = __half22float2(__hmul2(f10, a)), p11 = __half22float2(__hmul2(f11, b));
-  const __half2 o0 = __floats2half2_rn(p00.x + p01.x, p00.y + p01.y);
-  const __half2 o1 = __floats2half2_rn(p10.x + p11.x, p10.y + p11.y);
+  // the CPU sum starts from +0: (0 + p0) + p1, so -0 + -0 gives +0 as there
+  const __half2 o0 = __floats2half2_rn(__fadd_rn(__fadd_rn(0.f, p00.x), p01.x), __fadd_rn(__fadd_rn(0.f, p00.y), p01.y));
+  const __half2 o1 = __floats2half2_rn(__fadd_rn(__fadd_rn(0.f, p10.x), p11.x), __fadd_rn(__fadd_rn(0.f, p10.y), p11.y));
   x0 = static_cast<uint32_t>(__half_as_ushort(__low2half(o0))) |
        (static_cast<uint32_t>(__half_as_ushort(__high2half(o0))) << 16);
   x1 = static_cast<uint32_t>(__half_as_ushort(__low2half(o1))) |
