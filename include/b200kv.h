@@ -110,6 +110,20 @@ B200KV_API int b200kv_stick_relayout(const void *src, void *dst, int32_t elem_by
 
 /* Bytes a layout occupies on the device: 128 B per stick times the product of
  * the non-stick device dims (spyre_tensor_impl.cpp:287-293). */
+/* Restickify: moves a tensor that lives in device layout (src_device_size,
+ * src_stride_map) into device layout (dst_device_size, dst_stride_map) of the
+ * same host tensor (host_size, contiguous strides), on the device in one
+ * pass; destination padding is zero.  Replaces spyre::restickify
+ * (torch_spyre/_inductor/customops.py:338-342), whose target layouts come
+ * from restickify_device_size / restickify_stride_map
+ * (torch_spyre/_inductor/pass_utils.py:749-781).  Bit-exact. */
+B200KV_API int b200kv_stick_restickify(const void *src, void *dst, int32_t elem_bytes,
+                                       int32_t host_rank, const int64_t *host_size,
+                                       int32_t src_rank, const int64_t *src_device_size,
+                                       const int64_t *src_stride_map, int32_t dst_rank,
+                                       const int64_t *dst_device_size,
+                                       const int64_t *dst_stride_map, void *stream);
+
 B200KV_API int64_t b200kv_device_size_in_bytes(const int64_t *device_size,
                                     int32_t device_rank);
 

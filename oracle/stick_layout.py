@@ -130,3 +130,12 @@ def from_device(buf: np.ndarray, host_size, device_size, stride_map, dtype=None)
 def device_size_in_bytes(device_size):
     """128 bytes per stick times the number of sticks (spyre_tensor_impl.cpp:287-293)."""
     return int(np.prod(device_size[:-1])) * STICK_BYTES
+
+
+def restickify(buf: np.ndarray, host_size, src_device_size, src_stride_map, dst_device_size,
+               dst_stride_map) -> np.ndarray:
+    """Device buffer of layout dst holding what `buf` holds in layout src: read
+    back through src's element map, written through dst's (the data movement
+    of spyre::restickify, torch_spyre/_inductor/customops.py:338-342)."""
+    host = from_device(buf, host_size, src_device_size, src_stride_map, dtype=buf.dtype)
+    return to_device(host, dst_device_size, dst_stride_map)

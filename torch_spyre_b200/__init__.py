@@ -8,8 +8,8 @@ is loaded on first use and is the only implementation.
 from . import _lib, fp8, layout, ops, workloads  # noqa: F401
 from ._lib import B200KVError
 from .fp8 import dequantize_fp8_with_scale, empty_pool_fp8, pool_shape_fp8, quantize_fp8_with_scale
-from .layout import (SpyreTensorLayout, empty_pool, from_device_layout, page_layout, pool_shape, stick_layout,
-                     to_device_layout)
+from .layout import (SpyreTensorLayout, empty_pool, from_device_layout, page_layout, pool_shape, restickify,
+                     restickify_layout, stick_layout, to_device_layout)
 from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout, rope,
                   sdpa_decode)
 
@@ -30,6 +30,8 @@ __all__ = [
     "pool_shape",
     "pool_shape_fp8",
     "quantize_fp8_with_scale",
+    "restickify",
+    "restickify_layout",
     "rope",
     "sdpa_decode",
     "stick_layout",

@@ -58,6 +58,7 @@ SIGNATURES = {
         ctypes.c_int,
         [_p, _p, _i32, _i32, _p, _p, _i32, _p, _p, _i32, _p],
     ),
+    "b200kv_stick_restickify": (ctypes.c_int, [_p, _p, _i32, _i32, _p, _i32, _p, _p, _i32, _p, _p, _p]),
     "b200kv_decode_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "b200kv_decode_attention_f16": (
         ctypes.c_int,

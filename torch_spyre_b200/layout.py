@@ -181,3 +181,72 @@ def from_device_layout(buf: torch.Tensor, stl: SpyreTensorLayout, host_size, out
         out = torch.empty(tuple(host_size), dtype=buf.dtype, device=buf.device)
     _stick_relayout(buf, out, out, stl, 1)
     return out
+
+
+def _walked_host_dim(stride: int, host_size, cstride) -> Optional[int]:
+    """The host dim a device dim of stride-map entry `stride` walks (the size > 1
+    dim with the largest contiguous stride <= stride; None if there is none)."""
+    best = None
+    for d, (n, cs) in enumerate(zip(host_size, cstride)):
+        if n != 1 and cs <= stride and (best is None or cs > cstride[best]):
+            best = d
+    return best
+
+
+def restickify_layout(stl: SpyreTensorLayout, host_size, new_stick_dim: int) -> SpyreTensorLayout:
+    """The layout that results from moving stl's stick to host dim
+    ``new_stick_dim`` of a contiguous host tensor of ``host_size``.
+
+    Follows the reference's restickify_device_size / restickify_stride_map
+    (torch_spyre/_inductor/pass_utils.py:749-781): the stick dim becomes a full
+    stick of the new dim, the old stick's outer device dim counts sticks of the
+    new dim, and the device dim that walked the new dim now walks the old stick
+    dim.
+    """
+    host_size = list(host_size)
+    cstride, acc = [0] * len(host_size), 1
+    for d in range(len(host_size) - 1, -1, -1):
+        cstride[d] = acc
+        acc *= host_size[d]
+    dev, smap = list(stl.device_size), list(stl.stride_map)
+    old_sd = _walked_host_dim(smap[-1], host_size, cstride)
+    if old_sd is None or old_sd == new_stick_dim:
+        raise ValueError("the stick already walks that dim, or the layout has no stick dim")
+    walks = [_walked_host_dim(smap[j], host_size, cstride) if smap[j] > 0 and dev[j] > 1 else None
+             for j in range(len(dev) - 1)]
+    # the device dim counting sticks of the old stick dim; when it has size one
+    # (a single stick) nothing walks it and a size-one device dim stands in
+    old_outer = next((j for j, d in enumerate(walks) if d == old_sd),
+                     next((j for j in range(len(dev) - 1) if dev[j] == 1), None))
+    new_outer = next((j for j, d in enumerate(walks) if d == new_stick_dim), None)
+    if old_outer is None or new_outer is None:
+        raise ValueError("no device dim walks the old stick dim or the new stick dim")
+    stick = dev[-1]
+    new_dev = list(dev)
+    new_dev[-1] = stick
+    new_dev[old_outer] = -(-host_size[new_stick_dim] // stick)
+    new_dev[new_outer] = host_size[old_sd]
+    new_smap = list(smap)
+    new_smap[-1] = cstride[new_stick_dim]
+    new_smap[old_outer] = cstride[new_stick_dim] * stick
+    new_smap[new_outer] = cstride[old_sd]
+    return SpyreTensorLayout(new_dev, new_smap, stl.device_dtype)
+
+
+def restickify(buf: torch.Tensor, src: SpyreTensorLayout, dst: SpyreTensorLayout, host_size) -> torch.Tensor:
+    """The device buffer of layout ``dst`` holding the tensor that ``buf`` holds
+    in layout ``src`` (the reference's ``spyre::restickify``,
+    torch_spyre/_inductor/customops.py:338-342), moved on the device in one
+    pass; destination padding is zero."""
+    if buf.device.type != "cuda":
+        raise RuntimeError("restickify runs on CUDA devices only (there is no CPU fallback)")
+    out = torch.empty(dst.device_numel(), dtype=buf.dtype, device=buf.device)
+    hs, hs_p = _arr64(list(host_size))
+    sd, sd_p = _arr64(src.device_size)
+    ss, ss_p = _arr64(src.stride_map)
+    dd, dd_p = _arr64(dst.device_size)
+    ds, ds_p = _arr64(dst.stride_map)
+    _lib.call("b200kv_stick_restickify", buf.data_ptr(), out.data_ptr(), buf.element_size(), len(host_size), hs_p,
+              len(src.device_size), sd_p, ss_p, len(dst.device_size), dd_p, ds_p,
+              torch.cuda.current_stream(buf.device).cuda_stream)
+    return out
