@@ -485,34 +485,44 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None):
 
     up_stream, down_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
-    def pipelined_round():
+    pipe_rounds = max(1, -(-8 // n_sets))  # rounds of n_sets steps per captured graph
+
+    def pipelined_rounds():
         # the serving pipeline: every step's inputs go up on a copy stream and
-        # its result comes down on another, so step i + 1's upload and step
-        # i - 1's download overlap step i's compute (n_sets staging buffers)
+        # its result comes down on another, so the next steps' uploads and the
+        # previous steps' downloads overlap this step's compute; set i's next
+        # upload waits until its previous step has read the staged inputs
         cur = torch.cuda.current_stream(device)
         up_stream.wait_stream(cur)
         down_stream.wait_stream(cur)
-        landed = []
-        for i in range(n_sets):
-            host, dev = staged[i][0], staged[i][1]
-            with torch.cuda.stream(up_stream):
-                dev.copy_(host, non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(up_stream)
-            landed.append(ev)
-        for i in range(n_sets):
-            cur.wait_event(landed[i])
-            o = compute(i)
-            done = torch.cuda.Event()
-            done.record(cur)
-            with torch.cuda.stream(down_stream):
-                down_stream.wait_event(done)
-                staged[i][3].copy_(o, non_blocking=True)
+        read = [None] * n_sets
+        keep = []
+        for _ in range(pipe_rounds):
+            landed = []
+            for i in range(n_sets):
+                host, dev = staged[i][0], staged[i][1]
+                with torch.cuda.stream(up_stream):
+                    if read[i] is not None:
+                        up_stream.wait_event(read[i])
+                    dev.copy_(host, non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(up_stream)
+                landed.append(ev)
+            for i in range(n_sets):
+                cur.wait_event(landed[i])
+                o = compute(i)
+                keep.append(o)
+                done = torch.cuda.Event()
+                done.record(cur)
+                read[i] = done
+                with torch.cuda.stream(down_stream):
+                    down_stream.wait_event(done)
+                    staged[i][3].copy_(o, non_blocking=True)
         cur.wait_stream(up_stream)
         cur.wait_stream(down_stream)
 
-    def timed(run):
-        rounds = n // n_sets
+    def timed(run, steps_per_run):
+        rounds = max(1, n // steps_per_run)
         with torch.cuda.stream(stream):
             for _ in range(max(2, warmup // (4 * n_sets))):
                 run()
@@ -524,9 +534,9 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None):
                 run()
             b.record(stream)
             stream.synchronize()
-        return max_over_ranks(a.elapsed_time(b), world) / n
+        return max_over_ranks(a.elapsed_time(b), world) / (rounds * steps_per_run)
 
-    eager_ms = timed(eager_round)
+    eager_ms = timed(eager_round, n_sets)
     graph_ms = None
     if not (tp and world > 1) or ar is not None:
         # the same public-API steps captured once and replayed: every replay
@@ -535,12 +545,15 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None):
         with torch.cuda.stream(stream):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                pipelined_round()
-        graph_ms = timed(g.replay)
+                pipelined_rounds()
+        graph_ms = timed(g.replay, n_sets * pipe_rounds)
     ms = graph_ms if graph_ms is not None else eager_ms
     tokens = B if tp else B * world
     return {"value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": round(ms, 5),
+            "d2h_bytes_per_step": d2h,
+            "steps": (max(1, n // (n_sets * pipe_rounds)) * n_sets * pipe_rounds if graph_ms is not None
+                      else max(1, n // n_sets) * n_sets),
+            "ms_per_step": round(ms, 5),
             "path": ("torch.ops.b200kv.decode_attention_append (tp70b: kv_append + decode_attention + o_proj"
                      " + all-reduce) with pinned host buffers, "
                      + ("captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
