@@ -390,26 +390,22 @@ __device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item
 // output dims l, l + 32, l + 64, l + 96 of every head of the pair.  Splits are
 // read two at a time (every load of a batch issued before any is used) and
 // folded into a running (max, sum, accumulator) per head, so any number of
-// splits merges without shared memory.
+// splits merges without shared memory.  The running state starts from
+// (M, Ls, acc): empty for the ticket holder, or the merged state of a piece
+// that knows it is the pair's last, which then skips its own slot (`skip`;
+// -1 skips none).
 template <int G>
-__device__ __forceinline__ void combine_online_warp(const DecodeArgs &a, int b, int kvh,
-                                                    const SlotMap &sm, int lane) {
-  float M[G], Ls[G], acc[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    M[g] = -CUDART_INF_F;
-    Ls[g] = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[g][k] = 0.f;
-  }
+__device__ __forceinline__ void combine_online_warp_from(const DecodeArgs &a, int b, int kvh, const SlotMap &sm,
+                                                         int lane, int skip, float (&M)[G], float (&Ls)[G],
+                                                         float (&acc)[G][4]) {
   const int ns = sm.n();
   for (int s0 = 0; s0 < ns; s0 += 2) {
     float2 ml[2][G];
     float ov[2][G][4];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const bool in = s0 + j < ns;
-      const int64_t slot = sm(in ? s0 + j : s0);
+      const bool in = s0 + j < ns && sm(s0 + j) != skip;
+      const int64_t slot = sm(s0 + j < ns ? s0 + j : s0);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         ml[j][g] = in ? __ldcg(a.part_ml + slot * G + g) : make_float2(-CUDART_INF_F, 0.f);
@@ -441,6 +437,20 @@ __device__ __forceinline__ void combine_online_warp(const DecodeArgs &a, int b, 
     for (int k = 0; k < 4; ++k) store_out(a, b, h0 + g, lane + 32 * k, acc[g][k], Ls[g]);
     if (lane == 0) store_lse(a, b, h0 + g, M[g], Ls[g]);
   }
+}
+
+template <int G>
+__device__ __forceinline__ void combine_online_warp(const DecodeArgs &a, int b, int kvh,
+                                                    const SlotMap &sm, int lane) {
+  float M[G], Ls[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    M[g] = -CUDART_INF_F;
+    Ls[g] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[g][k] = 0.f;
+  }
+  combine_online_warp_from<G>(a, b, kvh, sm, lane, -1, M, Ls, acc);
 }
 
 }  // namespace b200kv

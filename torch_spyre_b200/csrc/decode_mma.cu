@@ -73,7 +73,7 @@ constexpr int kQSlotBytes = 8 * kQRowBytes;
 // every warp's unnormalised O^T [128 d][8 h], its (max, sum) per head and the
 // piece's identity.  Two buffers let the consumers run a piece ahead.
 struct PieceHeader {
-  int b, kvh, pair, nsplit, slot, end;
+  int b, kvh, pair, nsplit, slot, end, tail;
 };
 constexpr int kPieceO = 0;                                   // float [4][128][8]
 constexpr int kPieceML = kConsumerWarps * kHeadDim * 8 * 4;  // float2 [4][8]
@@ -105,6 +105,7 @@ constexpr int kDescLast = 2;   // last page of a piece
 constexpr int kDescPage = 4;   // the stage holds a page (an empty sequence has none)
 constexpr int kDescEnd = 8;    // no more work for this CTA
 constexpr int kDescNew = 16;   // the stage carries the appended token's K/V rows
+constexpr int kDescTail = 32;  // the page belongs to the CTA's final piece
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -132,6 +133,11 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -209,6 +215,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       for (int u = u_lo; u < u_hi;) {
         const Piece pc = locate_piece(a, pl, P, u, u_hi, owner);
         u = pc.u_next;
+        const int tail_flag = u >= u_hi ? kDescTail : 0;
         const int npages = pc.p_end - pc.p;
         const int nstages = max(npages, 1);  // an empty sequence still takes one stage
         for (int base = 0; base < nstages; base += 32) {
@@ -234,7 +241,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               const bool app = kAppend && has && (pc.ctx - 1) / kPageTokens == pc.p + i;
               if (kAppend) d.blk = (raw >= 0 && raw < a.num_blocks) ? raw : -1;
               d.flags = (i == 0 ? kDescFirst : 0) | (i == nstages - 1 ? kDescLast : 0) |
-                        (has ? kDescPage : 0) | (app ? kDescNew : 0);
+                        (has ? kDescPage : 0) | (app ? kDescNew : 0) | tail_flag;
               uint32_t tx = has ? 2 * L::kPage : 0;
               if (has && i == 0) tx += G * kHeadDim * 2;
               if (app) tx += 2 * kHeadDim * 2;
@@ -326,6 +333,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           for (int kk = 0; kk < 4; ++kk) store_out(a, hd.b, h0 + g, lane + 32 * kk, acc[g][kk], ls[g]);
           if (lane == 0) store_lse(a, hd.b, h0 + g, mx[g], ls[g]);
         }
+        continue;
+      }
+      // every other piece of the pair already in (their partials stored and
+      // fenced before their tickets): this piece is the last, so it merges
+      // its own state with their partials at once -- no store, fence, ticket
+      // or reload of its own partial.  Each lane's acquire load sees the
+      // counter; any lane that saw less sends the piece down the ticket path.
+      // (tried on the CTA's final piece only: the pair it starts was finished
+      // early by the next CTA, so it is almost always the pair's last)
+      if (hd.tail && __all_sync(0xffffffffu, ld_acquire_gpu(a.counters + hd.pair) == hd.nsplit - 1)) {
+        int pj, w;
+        pair_units(a, pl, hd.pair, &pj, &w);
+        combine_online_warp_from<G>(a, hd.b, hd.kvh, pair_slots(P, hd.pair, pj, w), lane, hd.slot, mx, ls, acc);
+        if (lane == 0) atomicExch(a.counters + hd.pair, 0);
         continue;
       }
       float *po = a.part_o + static_cast<int64_t>(hd.slot) * G * kHeadDim;
@@ -420,6 +441,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       hd->nsplit = d.nsplit;
       hd->slot = d.slot;
       hd->end = end;
+      hd->tail = (d.flags & kDescTail) != 0;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&pfull[pb]);
