@@ -145,6 +145,24 @@ B200KV_API int64_t b200kv_device_size_in_bytes(const int64_t *device_size,
 B200KV_API int64_t b200kv_decode_workspace_bytes(int64_t batch, int64_t num_q_heads,
                                       int64_t num_kv_heads, int64_t head_dim);
 
+/* Same as b200kv_decode_workspace_bytes (the name of the build contract). */
+B200KV_API int64_t b200kv_query_workspace_bytes(int64_t batch, int64_t num_q_heads,
+                                                int64_t num_kv_heads, int64_t head_dim);
+
+/* Merge of attention outputs over disjoint KV sets through their
+ * log-sum-exps (the split-KV combine, exposed): part_o [num_parts][rows]
+ * [head_dim] (fp16 when part_elem_bytes is 2, fp32 when 4), part_lse fp32
+ * [num_parts][rows] (natural log, -inf for an empty part) ->
+ * out fp16 [rows][head_dim] = sum_i exp(lse_i - m) o_i / sum_i exp(lse_i - m)
+ * and, when lse_out is not NULL, lse_out fp32 [rows] = m + log(sum_i ...).
+ * Rows whose parts are all empty give zeros and -inf.  Replaces nothing in
+ * the reference (it has no split KV); it lets a caller decode a shared
+ * prefix and per-sequence pages separately and merge the results. */
+B200KV_API int b200kv_lse_combine_f32(const void *part_o, int32_t part_elem_bytes,
+                                      const float *part_lse, int64_t num_parts, int64_t rows,
+                                      int64_t head_dim, void *out, float *lse_out,
+                                      void *stream);
+
 /*
  * q            fp16, element (b, h, d) at q[b * q_stride_b + h * q_stride_h + d]
  * k_pool/v_pool fp16 [num_blocks, num_kv_heads, D/64, 64, 64] (16-byte aligned)

@@ -10,8 +10,8 @@ from ._lib import B200KVError
 from .fp8 import dequantize_fp8_with_scale, empty_pool_fp8, pool_shape_fp8, quantize_fp8_with_scale
 from .layout import (SpyreTensorLayout, empty_pool, from_device_layout, page_layout, pool_shape, restickify,
                      restickify_layout, stick_layout, to_device_layout)
-from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout, rope,
-                  sdpa_decode)
+from .ops import (decode_attention, decode_attention_append, kv_append, kv_relayout, kv_unrelayout,
+                  merge_attention_states, rope, scaled_dot_product_fused_attention_overrideable, sdpa_decode)
 
 __all__ = [
     "B200KVError",
@@ -26,6 +26,7 @@ __all__ = [
     "kv_append",
     "kv_relayout",
     "kv_unrelayout",
+    "merge_attention_states",
     "page_layout",
     "pool_shape",
     "pool_shape_fp8",
@@ -33,6 +34,7 @@ __all__ = [
     "restickify",
     "restickify_layout",
     "rope",
+    "scaled_dot_product_fused_attention_overrideable",
     "sdpa_decode",
     "stick_layout",
 ]

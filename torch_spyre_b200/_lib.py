@@ -60,6 +60,8 @@ SIGNATURES = {
     ),
     "b200kv_stick_restickify": (ctypes.c_int, [_p, _p, _i32, _i32, _p, _i32, _p, _p, _i32, _p, _p, _p]),
     "b200kv_decode_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
+    "b200kv_query_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
+    "b200kv_lse_combine_f32": (ctypes.c_int, [_p, _i32, _p, _i64, _i64, _i64, _p, _p, _p]),
     "b200kv_decode_attention_f16": (
         ctypes.c_int,
         [

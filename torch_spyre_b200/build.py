@@ -30,6 +30,7 @@ SOURCES = [
     "fp8_ops.cu",
     "peer_allreduce.cu",
     "rope.cu",
+    "lse_combine.cu",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -45,6 +45,12 @@ extern "C" int64_t b200kv_decode_workspace_bytes(int64_t batch, int64_t num_q_he
   return workspace_layout(batch, num_q_heads, num_kv_heads).total;
 }
 
+// The name the build contract gives the workspace query (same arguments).
+extern "C" int64_t b200kv_query_workspace_bytes(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                                int64_t head_dim) {
+  return b200kv_decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim);
+}
+
 static int decode_entry(
     const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool, const void *v_pool,
     const int32_t *block_table, int64_t block_table_stride, const int32_t *context_lens, void *out,

@@ -450,7 +450,86 @@ def kv_unrelayout(pool, block_ids, num_tokens: int, error_flag=None) -> torch.Te
     return torch.ops.b200kv.kv_unrelayout(pool, block_ids, int(num_tokens), error_flag)
 
 
+# ------------------------------------------------------ merge split states --
+def merge_attention_states(outs, lses):
+    """Merges attention outputs computed over disjoint KV sets of the same
+    queries: outs [n] of [..., D] (fp16 or fp32), lses [n] of [...] fp32
+    (natural-log LSE, -inf for an empty set) -> (out fp16 [..., D], lse fp32).
+    E.g. a shared prefix decoded once and each sequence's own pages decoded
+    separately (``b200kv_lse_combine_f32``)."""
+    outs, lses = list(outs), list(lses)
+    if not outs or len(outs) != len(lses):
+        raise ValueError("need matching non-empty lists of outputs and LSEs")
+    o = torch.stack([t.contiguous() for t in outs])
+    l = torch.stack([t.contiguous().float() for t in lses])
+    _require_cuda(o, l)
+    if o.dtype not in (torch.float16, torch.float32):
+        raise ValueError("outputs must be fp16 or fp32")
+    D = o.shape[-1]
+    rows = o[0].numel() // D
+    if l[0].numel() != rows:
+        raise ValueError("each LSE must have one value per output row")
+    out = torch.empty(o.shape[1:], dtype=torch.float16, device=o.device)
+    lse = torch.empty(l.shape[1:], dtype=torch.float32, device=o.device)
+    _lib.call("b200kv_lse_combine_f32", o.data_ptr(), o.element_size(), l.data_ptr(), o.shape[0], rows, D,
+              out.data_ptr(), lse.data_ptr(), _stream_ptr(o.device))
+    return out, lse
+
+
 # ------------------------------------------------------------ SDPA adapter --
+def scaled_dot_product_fused_attention_overrideable(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    attn_bias: Optional[torch.Tensor] = None,
+    dropout_p: float = 0.0,
+    is_causal: bool = False,
+    return_debug_mask: bool = False,
+    scale: Optional[float] = None,
+):
+    """The decode case of ``aten::_scaled_dot_product_fused_attention_overrideable``
+    with the reference decomposition's signature and return tuple
+    (torch_spyre/_inductor/decompositions.py:523-611):
+    ``(out, logsumexp, None, None, max_q, max_k, philox_seed, philox_offset, None)``,
+    out [B, Hq, 1, D] in [B, 1, Hq, D] memory order.  The logsumexp the
+    reference leaves uninitialised is filled with the real one.  Query length
+    must be 1; dropout, an attention bias and a causal mask (which for one
+    query position would keep only key 0) are rejected.
+    """
+    if dropout_p > 0.0:
+        raise NotImplementedError("attention dropout is not implemented (as in the reference)")
+    if attn_bias is not None:
+        raise NotImplementedError("an attention bias is not supported by the paged decode path")
+    if query.dim() != 4 or query.shape[2] != 1:
+        raise NotImplementedError("only the decode case (one query position) is implemented")
+    if is_causal and key.shape[2] != 1:
+        raise NotImplementedError("is_causal with one query position masks every key but the first")
+    B, Hq, _, D = query.shape
+    Hkv, S = key.shape[1], key.shape[2]
+    out, lse = _sdpa_decode_with_lse(query, key, value, scale, Hq != Hkv)
+    seed = torch.empty((1,), dtype=torch.float16, device=query.device)
+    offset = torch.empty((1,), dtype=torch.float16, device=query.device)
+    return out, lse.view(B, Hq, 1), None, None, 1, S, seed, offset, None
+
+
+def _sdpa_decode_with_lse(query, key, value, scale, enable_gqa):
+    B, Hq, _, D = query.shape
+    Hkv, S = key.shape[1], key.shape[2]
+    if Hq != Hkv and not enable_gqa:
+        raise ValueError("Hq != Hkv requires enable_gqa=True")
+    nblk = max(1, -(-S // PAGE_TOKENS))
+    k_pool = torch.empty((B * nblk, Hkv, D // 64, PAGE_TOKENS, 64), dtype=torch.float16, device=query.device)
+    v_pool = torch.empty_like(k_pool)
+    block_table = torch.arange(B * nblk, dtype=torch.int32, device=query.device).view(B, nblk)
+    for b in range(B):
+        ids = block_table[b]
+        kv_relayout(key[b].transpose(0, 1).contiguous(), k_pool, ids)
+        kv_relayout(value[b].transpose(0, 1).contiguous(), v_pool, ids)
+    ctx = torch.full((B,), S, dtype=torch.int32, device=query.device)
+    out, lse = decode_attention(query[:, :, 0, :], k_pool, v_pool, block_table, ctx, scale=scale, return_lse=True)
+    # [B, Hq, D] -> [B, 1, Hq, D] memory order, viewed as [B, Hq, 1, D]
+    return out.unsqueeze(1).transpose(1, 2), lse
+
 def sdpa_decode(
     query: torch.Tensor,
     key: torch.Tensor,
@@ -468,20 +547,4 @@ def sdpa_decode(
     """
     if query.dim() != 4 or query.shape[2] != 1:
         raise ValueError("sdpa_decode handles one query position: query must be [B, Hq, 1, D]")
-    B, Hq, _, D = query.shape
-    Hkv, S = key.shape[1], key.shape[2]
-    if Hq != Hkv and not enable_gqa:
-        raise ValueError("Hq != Hkv requires enable_gqa=True")
-    nblk = max(1, -(-S // PAGE_TOKENS))
-    k_pool = torch.empty((B * nblk, Hkv, D // 64, PAGE_TOKENS, 64), dtype=torch.float16, device=query.device)
-    v_pool = torch.empty_like(k_pool)
-    block_table = torch.arange(B * nblk, dtype=torch.int32, device=query.device).view(B, nblk)
-    for b in range(B):
-        ids = block_table[b]
-        kv_relayout(key[b].transpose(0, 1).contiguous(), k_pool, ids)
-        kv_relayout(value[b].transpose(0, 1).contiguous(), v_pool, ids)
-    ctx = torch.full((B,), S, dtype=torch.int32, device=query.device)
-    q3 = query[:, :, 0, :]
-    out = decode_attention(q3, k_pool, v_pool, block_table, ctx, scale=scale)
-    # [B, Hq, D] -> [B, 1, Hq, D] memory order, viewed as [B, Hq, 1, D]
-    return out.unsqueeze(1).transpose(1, 2)
+    return _sdpa_decode_with_lse(query, key, value, scale, enable_gqa)[0]
