@@ -437,6 +437,28 @@ B200KV_API int b200kv_peer_allreduce_f16(void *const *peer_buffers, int32_t rank
                                          int64_t capacity_elems, int32_t ctas,
                                          int32_t *error_flag, void *stream);
 
+/* Fused o_proj GEMM + SUM all-reduce of the tensor-parallel step, one kernel
+ * per rank: out[b, n] = sum over ranks of sum_k attn[b, k] * w[n, k]
+ * (attn fp16 [batch, k] row stride attn_stride_b; w fp16 [hidden, k] row
+ * stride w_stride_n, the rank's input columns of W_o; out fp16 [batch, hidden]
+ * row stride out_stride_b), with the peer buffers of b200kv_peer_alloc
+ * (capacity >= 128 * hidden).  Each rank's partial is rounded to fp16, the
+ * partials are summed in fp32 in rank order and rounded once, as
+ * b200kv_peer_allreduce_f16 does.  The GEMM runs on the tensor cores
+ * (tcgen05, fp32 accumulate); each 128 x 64 output tile is exchanged as soon
+ * as it is computed.  batch <= 128, k a multiple of 64, hidden a multiple of
+ * 64 * world and at most 64 * (SM count).  Replaces the o_proj + allreduce
+ * pair of the reference's TP step (SpyreCCLBackend::allreduce,
+ * torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494).  Shares the peer
+ * buffers' epoch with b200kv_peer_allreduce_f16 (calls of both kinds may
+ * interleave, in the same order on every rank). */
+B200KV_API int b200kv_oproj_allreduce_f16(const void *attn, int64_t attn_stride_b, const void *w,
+                                          int64_t w_stride_n, void *out, int64_t out_stride_b,
+                                          int64_t batch, int64_t hidden, int64_t k,
+                                          void *const *peer_buffers, int32_t rank, int32_t world,
+                                          int64_t capacity_elems, int32_t *error_flag,
+                                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

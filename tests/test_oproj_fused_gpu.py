@@ -1,0 +1,49 @@
+"""Fused o_proj GEMM + all-reduce (b200kv_oproj_allreduce_f16), single rank:
+the tcgen05 GEMM against an fp32 reference (2e-2 abs / 1e-2 rel on fp16
+outputs of K up to 8192 products) and against cuBLAS; plus the host checks.
+The 2-rank exchange is tested in test_peer_allreduce_gpu.py."""
+
+import pytest
+import torch
+
+from torch_spyre_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(B, N, K, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    attn = torch.randn((B, K), generator=g, device="cuda", dtype=torch.float16)
+    w = (torch.randn((N, K), generator=g, device="cuda", dtype=torch.float16) * 0.02)
+    return attn, w
+
+
+@pytest.mark.parametrize("B,N,K", [(128, 8192, 8192), (128, 8192, 1024), (5, 512, 1024), (128, 64, 64), (1, 128, 4096)])
+def test_single_rank_gemm(B, N, K):
+    from torch_spyre_b200.tp import PeerAllReduce
+
+    attn, w = _case(B, N, K, B + N + K)
+    ar = PeerAllReduce(128 * N)
+    out = ar.oproj_all_reduce(attn, w)
+    torch.cuda.synchronize()
+    assert int(ar.error_flag.item()) == 0
+    ref = (attn.float() @ w.float().t())
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(out.float(), torch.matmul(attn, w.t()).float(), atol=2e-2, rtol=1e-2)
+    # repeat calls (epochs advance) and a strided attn view
+    big = torch.zeros((B, K + 64), device="cuda", dtype=torch.float16)
+    big[:, 32:32 + K] = attn
+    out2 = ar.oproj_all_reduce(big[:, 32:32 + K], w)
+    assert torch.equal(out2, out)
+    ar.close()
+
+
+def test_host_checks():
+    lib = _lib.lib()
+    import ctypes
+
+    table = (ctypes.c_void_p * 1)(1 << 20)
+    args = [1 << 21, 1024, 1 << 22, 1024, 1 << 23, 512, 128, 512, 1024, table, 0, 1, 128 * 512, None, None]
+    assert lib.b200kv_oproj_allreduce_f16(*[a if i != 8 else 1000 for i, a in enumerate(args)]) == 1  # k % 64
+    assert lib.b200kv_oproj_allreduce_f16(*[a if i != 6 else 200 for i, a in enumerate(args)]) == 1   # batch
+    assert lib.b200kv_oproj_allreduce_f16(*[a if i != 12 else 64 for i, a in enumerate(args)]) == 1   # capacity

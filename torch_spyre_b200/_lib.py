@@ -147,6 +147,10 @@ SIGNATURES = {
             _p, _p,  # error_flag, stream
         ],
     ),
+    "b200kv_oproj_allreduce_f16": (
+        ctypes.c_int,
+        [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i64, _p, _p],
+    ),
     "b200kv_peer_buffer_bytes": (_i64, [_i64, _i32]),
     "b200kv_peer_alloc": (ctypes.c_int, [_i64, _i32, _p]),
     "b200kv_peer_free": (ctypes.c_int, [_p]),

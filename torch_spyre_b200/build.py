@@ -31,6 +31,7 @@ SOURCES = [
     "peer_allreduce.cu",
     "rope.cu",
     "lse_combine.cu",
+    "oproj_allreduce.cu",
 ]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -1,0 +1,371 @@
+// Fused o_proj GEMM + tensor-parallel all-reduce: out = sum over ranks of
+// attn_r [B, K] . W_r[N, K]^T, one kernel per rank.
+//
+// The reference's TP step is the o_proj of each rank's heads followed by a SUM
+// all-reduce of the [B, N] partial (SpyreCCLBackend::allreduce,
+// torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494).  Here every CTA owns
+// one 128 x 64 output tile (rows = the batch, zero-padded to 128 by the TMA):
+//   warp 4   TMA producer: K-slabs of attn (128 x 64) and W (64 x 64), 128-byte
+//            swizzle, into a kStages ring with full/empty mbarriers;
+//   warp 5   allocates 64 TMEM columns; one lane issues tcgen05.mma
+//            (kind::f16, M = 128, N = 64, K = 16, fp32 accumulate in TMEM) and
+//            tcgen05.commit frees each stage and finally signals the tile;
+//   warps 0-3  read the accumulator (tcgen05.ld, TMEM lane = row) and run the
+//            tile's all-reduce at once, so a tile's exchange overlaps the
+//            other tiles' GEMM: the tile is owned by rank tile / (T / N); a
+//            non-owner sends its fp16 partial rows to the owner, the owner
+//            sums the N partials (rank order, fp32, rounded once), writes its
+//            output rows and sends the sum to every other rank, which polls
+//            it into its output.
+// Transfers are the flagged 8-byte packets of peer_allreduce.cu (data + epoch,
+// receiver polls, no fences, no multicast) in the same peer buffers, receive
+// regions and epoch counter, so fused and unfused calls interleave.  All CTAs
+// (N / 64 <= 148) are resident at once, so no CTA waits on one that cannot
+// run.  Every wait is bounded (2 s); TMEM is freed on every path.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace b200kv {
+namespace {
+
+constexpr int kOpM = 128, kOpN = 64, kOpK = 64;
+constexpr int kOpStages = 6;
+constexpr int kOpATile = kOpM * kOpK * 2;  // 16 KiB
+constexpr int kOpBTile = kOpN * kOpK * 2;  // 8 KiB
+constexpr int kOpStage = kOpATile + kOpBTile;
+constexpr int kOpThreads = 192;
+constexpr int kOpMaxRanks = 8;
+constexpr int kOpPktPerRow = kOpN * 2 / 8;           // 16 packets of 8 data bytes per tile row
+constexpr int kOpPktPerTile = kOpM * kOpPktPerRow;   // 2048
+constexpr int kOpSmem = kOpStages * kOpStage + 1024 + 256;
+
+struct OpArgs {
+  uint8_t *peers[kOpMaxRanks];
+  int rank, world, tiles, batch;
+  int kblocks;
+  __half *out;
+  int64_t out_sb;
+  int64_t recv1_off, recv2_off, region_bytes, counter_off;
+  int32_t *error_flag;
+};
+
+// K-major operand tile of 128-byte rows in the 128-byte swizzle (8-row atoms
+// of 1024 bytes): start address >> 4, LBO 1 (unused for this layout), SBO
+// 1024 >> 4, descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t smem_addr) {
+  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both
+// K-major, N = 64, M = 128.
+constexpr uint32_t kOpIdesc = (1u << 4) | (uint32_t(kOpN >> 3) << 17) | (uint32_t(kOpM >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void st_volatile_v4(uint4 *p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// Polls packet p until both words carry `epoch` (bounded; `dead` stops it).
+__device__ __forceinline__ uint2 recv_pkt(const uint4 *p, uint32_t epoch, uint64_t t0, bool &dead, int32_t *err) {
+  uint4 v;
+  for (uint32_t i = 0;; ++i) {
+    v = ld_volatile_v4(p);
+    if ((v.y == epoch && v.w == epoch) || dead) break;
+    if ((i & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+      dead = true;
+      if (err) atomicOr(err, B200KV_DEVERR_TIMEOUT);
+      break;
+    }
+  }
+  return make_uint2(v.x, v.z);
+}
+
+__global__ void __launch_bounds__(kOpThreads, 1)
+    oproj_allreduce_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+                           const OpArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOpStages * kOpStage);
+  uint64_t *empty = full + kOpStages;
+  uint64_t *accum = empty + kOpStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+  uint32_t *epoch_slot = tmem_slot + 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x;
+  const int n0 = tile * kOpN;
+
+  if (tid == 0) {
+    prefetch_tensormap(&amap);
+    prefetch_tensormap(&wmap);
+    for (int s = 0; s < kOpStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+    *epoch_slot = static_cast<uint32_t>(*reinterpret_cast<volatile int32_t *>(a.peers[a.rank] + a.counter_off)) + 1u;
+  }
+  if (warp == 5) {  // 64 TMEM columns for the 128 x 64 fp32 accumulator
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(64)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t epoch = *epoch_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {  // producer
+      for (int kb = 0; kb < a.kblocks; ++kb) {
+        const int s = kb % kOpStages;
+        const uint32_t ph = (kb / kOpStages) & 1u;
+        mbar_wait_bounded(&empty[s], ph ^ 1u, a.error_flag);
+        mbar_arrive_expect_tx(&full[s], kOpStage);
+        uint8_t *st = smem + s * kOpStage;
+        tma_load_2d(st, &amap, &full[s], kb * kOpK, 0);
+        tma_load_2d(st + kOpATile, &wmap, &full[s], kb * kOpK, n0);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {  // MMA issuer
+      for (int kb = 0; kb < a.kblocks; ++kb) {
+        const int s = kb % kOpStages;
+        mbar_wait_bounded(&full[s], (kb / kOpStages) & 1u, a.error_flag);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t abase = smem_u32(smem + s * kOpStage), bbase = abase + kOpATile;
+#pragma unroll
+        for (int ki = 0; ki < kOpK / 16; ++ki) {
+          const uint64_t ad = kmajor_sw128_desc(abase + ki * 32), bd = kmajor_sw128_desc(bbase + ki * 32);
+          const uint32_t acc = (kb > 0 || ki > 0) ? 1u : 0u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+              "l"(ad), "l"(bd), "r"(kOpIdesc), "r"(acc)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&empty[s]))
+                     : "memory");
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                       smem_u32(accum))
+                   : "memory");
+    }
+  } else {
+    // ------------------------------------------------ epilogue: warps 0-3 --
+    mbar_wait_bounded(accum, 0, a.error_flag);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int row = warp * 32 + lane;
+    uint32_t r[64];
+    {
+      const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,"
+          "%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+            "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+            "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+            "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]),
+            "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
+            "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]),
+            "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]),
+            "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+          : "r"(taddr)
+          : "memory");
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    }
+    // this rank's partial row, rounded to fp16 (as the unfused path's GEMM
+    // output), 32 words of two halves
+    uint32_t h[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const __half2 v = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+      h[i] = *reinterpret_cast<const uint32_t *>(&v);
+    }
+    const bool live = row < a.batch;
+    const int N = a.world, me = a.rank;
+    const int per_owner = a.tiles / N;
+    const int owner = tile / per_owner, local = tile - owner * per_owner;
+    const int64_t par_off = int64_t(epoch & 1u) * a.region_bytes;
+    const int64_t slot_pk = int64_t(per_owner) * kOpPktPerTile;  // packets per source slot
+    const int64_t pk0 = int64_t(local) * kOpPktPerTile + int64_t(row) * kOpPktPerRow;
+    __half *orow = a.out + int64_t(row) * a.out_sb + n0;
+    const uint64_t t0 = global_timer_ns();
+    bool dead = false;
+    if (live) {
+      if (owner != me) {
+        // send the partial row to the owner, then take the sum back
+        uint4 *dst = reinterpret_cast<uint4 *>(a.peers[owner] + a.recv1_off + par_off) + int64_t(me) * slot_pk + pk0;
+#pragma unroll
+        for (int j = 0; j < kOpPktPerRow; ++j) st_volatile_v4(dst + j, make_uint4(h[2 * j], epoch, h[2 * j + 1], epoch));
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.peers[me] + a.recv2_off + par_off) + int64_t(owner) * slot_pk + pk0;
+#pragma unroll
+        for (int j = 0; j < kOpPktPerRow; ++j) {
+          const uint2 v = recv_pkt(src + j, epoch, t0, dead, a.error_flag);
+          *reinterpret_cast<uint2 *>(orow + 4 * j) = v;
+        }
+      } else {
+        // owner: sum the N partial rows in rank order, keep and send the sum
+        float acc[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+        for (int q = 0; q < N; ++q) {
+          const uint4 *src = reinterpret_cast<const uint4 *>(a.peers[me] + a.recv1_off + par_off) + int64_t(q) * slot_pk + pk0;
+#pragma unroll
+          for (int j = 0; j < kOpPktPerRow; ++j) {
+            const uint2 v = q == me ? make_uint2(h[2 * j], h[2 * j + 1]) : recv_pkt(src + j, epoch, t0, dead, a.error_flag);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+            acc[4 * j] += f0.x;
+            acc[4 * j + 1] += f0.y;
+            acc[4 * j + 2] += f1.x;
+            acc[4 * j + 3] += f1.y;
+          }
+        }
+        uint32_t s[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const __half2 v = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+          s[i] = *reinterpret_cast<const uint32_t *>(&v);
+        }
+#pragma unroll
+        for (int j = 0; j < kOpPktPerRow; ++j)
+          *reinterpret_cast<uint2 *>(orow + 4 * j) = make_uint2(s[2 * j], s[2 * j + 1]);
+        for (int q = 0; q < N; ++q) {
+          if (q == me) continue;
+          uint4 *dst = reinterpret_cast<uint4 *>(a.peers[q] + a.recv2_off + par_off) + int64_t(me) * slot_pk + pk0;
+#pragma unroll
+          for (int j = 0; j < kOpPktPerRow; ++j) st_volatile_v4(dst + j, make_uint4(s[2 * j], epoch, s[2 * j + 1], epoch));
+        }
+      }
+    }
+  }
+
+  // the last CTA to finish publishes the epoch; warp 5 frees the TMEM
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (tid == 0) {
+    int32_t *counter = reinterpret_cast<int32_t *>(a.peers[a.rank] + a.counter_off);
+    __threadfence();
+    if (atomicAdd(counter + 1, 1) == a.tiles - 1) {
+      counter[1] = 0;
+      __threadfence();
+      *reinterpret_cast<volatile int32_t *>(counter) = static_cast<int32_t>(epoch);
+    }
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64) : "memory");
+  }
+}
+
+int make_rowmajor_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t row_stride_elems,
+                      uint32_t box_rows) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return set_error(B200KV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kOpK), box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(B200KV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return B200KV_OK;
+}
+
+// The peer-buffer regions of peer_allreduce.cu (same layout function there).
+void peer_regions(int64_t capacity, int world, int64_t *recv1, int64_t *recv2, int64_t *region, int64_t *counter) {
+  auto up = [](int64_t x) { return (x + 255) & ~int64_t(255); };
+  const int64_t part_cap = (capacity + world - 1) / world;
+  *region = int64_t(world) * (part_cap / 4) * 16;
+  *recv1 = up(capacity * 2);
+  *recv2 = up(*recv1 + 2 * *region);
+  *counter = up(*recv2 + 2 * *region);
+}
+
+}  // namespace
+}  // namespace b200kv
+
+using namespace b200kv;
+
+extern "C" int b200kv_oproj_allreduce_f16(const void *attn, int64_t attn_stride_b, const void *w,
+                                          int64_t w_stride_n, void *out, int64_t out_stride_b, int64_t batch,
+                                          int64_t hidden, int64_t k, void *const *peer_buffers, int32_t rank,
+                                          int32_t world, int64_t capacity_elems, int32_t *error_flag,
+                                          void *stream) {
+  clear_error();
+  B200KV_CHECK_ARG(world >= 1 && world <= kOpMaxRanks, "world must be in [1, %d]", kOpMaxRanks);
+  B200KV_CHECK_ARG(rank >= 0 && rank < world, "rank %d outside [0, %d)", rank, world);
+  B200KV_CHECK_ARG(batch >= 0 && batch <= kOpM, "batch must be in [0, %d]", kOpM);
+  B200KV_CHECK_ARG(k > 0 && k % kOpK == 0, "k (%lld) must be a positive multiple of %d", (long long)k, kOpK);
+  B200KV_CHECK_ARG(hidden > 0 && hidden % (kOpN * world) == 0,
+                   "hidden (%lld) must be a multiple of %d * world", (long long)hidden, kOpN);
+  const int64_t tiles = hidden / kOpN;
+  int dev = 0, sms = 0;
+  int st = current_device_sm_count(&dev, &sms);
+  if (st != B200KV_OK) return st;
+  if (tiles > sms)
+    return set_error(B200KV_ERR_UNSUPPORTED, "hidden %lld needs %lld co-resident CTAs (> %d SMs)",
+                     (long long)hidden, (long long)tiles, sms);
+  B200KV_CHECK_ARG(capacity_elems >= int64_t(kOpM) * hidden && capacity_elems % (int64_t(world) * 8) == 0,
+                   "the peer buffers must hold 128 x hidden elements (capacity %lld)", (long long)capacity_elems);
+  if (batch == 0) return B200KV_OK;
+  B200KV_CHECK_ARG(attn && w && out && peer_buffers, "null pointer argument");
+  B200KV_CHECK_ARG((reinterpret_cast<uintptr_t>(attn) & 15u) == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0 &&
+                       attn_stride_b % 8 == 0 && w_stride_n % 8 == 0 && attn_stride_b >= k && w_stride_n >= k,
+                   "attn / w must be 16-byte aligned with row strides that are multiples of 8 elements >= k");
+  B200KV_CHECK_ARG((reinterpret_cast<uintptr_t>(out) & 7u) == 0 && out_stride_b % 4 == 0 && out_stride_b >= hidden,
+                   "out must be 8-byte aligned with a row stride that is a multiple of 4 elements >= hidden");
+  OpArgs a{};
+  for (int p = 0; p < world; ++p) {
+    B200KV_CHECK_ARG(peer_buffers[p] && (reinterpret_cast<uintptr_t>(peer_buffers[p]) & 255u) == 0,
+                     "peer buffer %d is null or not 256-byte aligned", p);
+    a.peers[p] = static_cast<uint8_t *>(peer_buffers[p]);
+  }
+  CUtensorMap am, wm;
+  st = make_rowmajor_map(&am, attn, batch, k, attn_stride_b, kOpM);
+  if (st != B200KV_OK) return st;
+  st = make_rowmajor_map(&wm, w, hidden, k, w_stride_n, kOpN);
+  if (st != B200KV_OK) return st;
+  a.rank = rank;
+  a.world = world;
+  a.tiles = static_cast<int>(tiles);
+  a.batch = static_cast<int>(batch);
+  a.kblocks = static_cast<int>(k / kOpK);
+  a.out = static_cast<__half *>(out);
+  a.out_sb = out_stride_b;
+  peer_regions(capacity_elems, world, &a.recv1_off, &a.recv2_off, &a.region_bytes, &a.counter_off);
+  a.error_flag = error_flag;
+  static int configured[64] = {0};
+  if (!__atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) {
+    B200KV_CUDA_TRY(cudaFuncSetAttribute(oproj_allreduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOpSmem));
+    __atomic_store_n(&configured[dev], 1, __ATOMIC_RELEASE);
+  }
+  oproj_allreduce_kernel<<<static_cast<int>(tiles), kOpThreads, kOpSmem, static_cast<cudaStream_t>(stream)>>>(am, wm, a);
+  B200KV_CUDA_TRY(cudaGetLastError());
+  return B200KV_OK;
+}

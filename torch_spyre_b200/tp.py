@@ -104,8 +104,10 @@ class PeerAllReduce:
         import torch.distributed as dist
 
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        self._dist = dist.is_initialized()
+        # without a process group: a single rank (the fused o_proj is then a plain GEMM)
+        self.rank = dist.get_rank(group) if self._dist else 0
+        self.world = dist.get_world_size(group) if self._dist else 1
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         q = 8 * self.world
         self.capacity = -(-int(capacity) // q) * q
@@ -119,7 +121,10 @@ class PeerAllReduce:
             handle = (ctypes.c_char * hbytes)()
             _lib.call("b200kv_ipc_get_handle", ctypes.c_void_p(self._own), handle)
             handles = [None] * self.world
-            dist.all_gather_object(handles, bytes(handle), group=group)
+            if self._dist:
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            else:
+                handles[0] = bytes(handle)
             self._opened = []
             ptrs = []
             for r, h in enumerate(handles):
@@ -151,6 +156,24 @@ class PeerAllReduce:
                   self.ctas, self.error_flag.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
         return t
 
+    def oproj_all_reduce(self, attn: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None
+                         ) -> torch.Tensor:
+        """Fused o_proj + all-reduce (b200kv_oproj_allreduce_f16): returns
+        sum over ranks of attn [B, K] @ w [N, K]^T as fp16 [B, N] (B <= 128),
+        the GEMM on the tensor cores and every 128 x 64 output tile exchanged
+        as soon as it is computed.  A collective, like ``all_reduce``."""
+        if attn.dtype != torch.float16 or w.dtype != torch.float16 or attn.dim() != 2 or w.dim() != 2:
+            raise ValueError("attn [B, K] and w [N, K] must be fp16 matrices")
+        if attn.stride(1) != 1 or w.stride(1) != 1 or attn.shape[1] != w.shape[1]:
+            raise ValueError("attn and w need unit column strides and the same K")
+        B, N = attn.shape[0], w.shape[0]
+        if out is None:
+            out = torch.empty((B, N), dtype=torch.float16, device=attn.device)
+        _lib.call("b200kv_oproj_allreduce_f16", attn.data_ptr(), attn.stride(0), w.data_ptr(), w.stride(0),
+                  out.data_ptr(), out.stride(0), B, N, attn.shape[1], self._table, self.rank, self.world,
+                  self.capacity, self.error_flag.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        return out
+
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (after a barrier:
         no peer may still write into it)."""
@@ -159,7 +182,8 @@ class PeerAllReduce:
         if self._own is None:
             return
         torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
+        if self._dist:
+            dist.barrier(group=self.group)
         self._data = None
         for p in self._opened:
             _lib.call("b200kv_ipc_close_handle", ctypes.c_void_p(p))
@@ -185,6 +209,7 @@ def tp_decode_step(
     k_scale: Optional[torch.Tensor] = None,
     v_scale: Optional[torch.Tensor] = None,
     allreduce: Optional[PeerAllReduce] = None,
+    fused_oproj: bool = False,
 ) -> torch.Tensor:
     """One rank's step: local decode -> o_proj partial -> SUM all-reduce.
 
@@ -192,7 +217,9 @@ def tp_decode_step(
     k_scale / v_scale are the dequantisation scales of fp8 pools.  With
     ``allreduce`` the partial is written into its peer buffer and reduced by
     the peer-memory kernel (the result is a view of that buffer, valid until
-    the next step); otherwise NCCL (``group``) reduces it.
+    the next step) or, with ``fused_oproj``, the o_proj GEMM and the
+    all-reduce run as one kernel (``PeerAllReduce.oproj_all_reduce``);
+    otherwise NCCL (``group``) reduces it.
     Every rank must call this in the same order (it contains one collective).
     """
     if attn_fn is None:
@@ -203,6 +230,8 @@ def tp_decode_step(
         attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens)
     B = attn.shape[0]
     flat = attn.reshape(B, -1)
+    if allreduce is not None and fused_oproj:
+        return allreduce.oproj_all_reduce(flat, w_o_local, out=out)
     if allreduce is not None:
         partial = allreduce.buffer((B, w_o_local.shape[0]))
         torch.matmul(flat, w_o_local.t(), out=partial)
