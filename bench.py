@@ -64,8 +64,9 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--kv-dtype", default="fp16", choices=["fp16", "fp8"],
                    help="KV page element type: fp16 (the reference's) or e4m3 pages with per-pool fp16 scales")
-    p.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
-                   help="tp70b at N > 1: the o_proj all-reduce as libb200kv's peer-memory kernel or NCCL")
+    p.add_argument("--allreduce", default="peer", choices=["peer", "fused", "nccl"],
+                   help="tp70b at N > 1: the o_proj all-reduce as libb200kv's peer-memory kernel, the fused "
+                        "o_proj GEMM + all-reduce kernel, or NCCL")
     p.add_argument("--nccl-graph", action="store_true",
                    help="tp70b at N > 1: capture the step, NCCL all-reduce included, in a CUDA graph")
     return p.parse_args()
@@ -258,7 +259,8 @@ def run_ours(args, rank, world, local):
                            dtype=torch.float16) * 0.02)
         partial = torch.empty((B, hidden), dtype=torch.float16, device=device)
     ar = None
-    if tp and world > 1 and args.allreduce == "peer":
+    fused = tp and world > 1 and args.allreduce == "fused"
+    if tp and world > 1 and args.allreduce in ("peer", "fused"):
         from torch_spyre_b200.tp import PeerAllReduce
 
         ar = PeerAllReduce(B * cfg.hidden, device=device)
@@ -266,8 +268,8 @@ def run_ours(args, rank, world, local):
     def step(s):
         if tp:
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
-                                  out=partial if ar is None else None, k_scale=s.k_scale, v_scale=s.v_scale,
-                                  allreduce=ar)
+                                  out=partial if ar is None or fused else None, k_scale=s.k_scale,
+                                  v_scale=s.v_scale, allreduce=ar, fused_oproj=fused)
         return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
                                     v_scale=s.v_scale)
 
@@ -370,7 +372,7 @@ def run_ours(args, rank, world, local):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar)
+        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar, fused)
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline_seconds > 0:
@@ -391,7 +393,8 @@ def run_ours(args, rank, world, local):
                    "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
                    "kv_heads_per_rank": sets[0].k_pool.shape[1], "kv_dtype": args.kv_dtype,
                    "parallelism": (f"tp{world} (kv-head shards + "
-                                   f"{'peer-memory' if ar is not None else 'NCCL'} all-reduce)" if tp
+                                   f"{'fused o_proj + peer-memory' if fused else 'peer-memory' if ar is not None else 'NCCL'}"
+                                   " all-reduce)" if tp
                                    else f"dp{world} (sequence shards)"),
                    "l2": f"{n_sets} rotating input sets, {kv_bytes / 1e6:.1f} MB KV read per step (L2 126 MB)",
                    "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")},
@@ -411,7 +414,7 @@ def run_ours(args, rank, world, local):
         ar.close()
 
 
-def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None):
+def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fused=False):
     """Public-API decode step with host buffers: H2D inputs, append, decode, D2H.
 
     Each step's inputs (q, the new token's K/V rows, its slots, the block table
@@ -470,7 +473,7 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None):
             shard = HeadShard(int(os.environ.get("RANK", "0")), world, cfg.num_q_heads, cfg.num_kv_heads,
                               cfg.head_dim)
             o = tp_decode_step(shard, v["q"], s.k_pool, s.v_pool, v["block_table"], v["context_lens"], w_o,
-                               k_scale=s.k_scale, v_scale=s.v_scale, allreduce=ar)
+                               k_scale=s.k_scale, v_scale=s.v_scale, allreduce=ar, fused_oproj=fused)
         else:  # one launch: append the new token's K/V rows and decode
             o = tsb.decode_attention_append(v["q"], v["k_new"], v["v_new"], s.k_pool, s.v_pool,
                                             v["block_table"], v["context_lens"], k_scale=s.k_scale,

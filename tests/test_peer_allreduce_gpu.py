@@ -186,3 +186,41 @@ def test_missing_peer_times_out_with_status():
     _, flag, x, timeout_bit = res[0]
     assert flag & timeout_bit
     assert x == 120.0 and res[1][2] == 120.0
+
+
+def _w_fused(rank, world, port, results):
+    dist = _init(rank, world, port)
+    from torch_spyre_b200.tp import PeerAllReduce
+
+    try:
+        B, N, K = 128, 8192, 2048
+        g = torch.Generator(device="cuda").manual_seed(100 + rank)
+        attn = torch.randn((B, K), generator=g, device="cuda", dtype=torch.float16)
+        w = torch.randn((N, K), generator=g, device="cuda", dtype=torch.float16) * 0.02
+        ar = PeerAllReduce(B * N)
+        fused = ar.oproj_all_reduce(attn, w).cpu()
+        # the unfused path on the same buffers (epochs interleave), then fused again
+        part = ar.buffer((B, N))
+        torch.matmul(attn, w.t(), out=part)
+        unfused = ar.all_reduce(part).cpu().clone()
+        fused2 = ar.oproj_all_reduce(attn[:77], w).cpu()
+        torch.cuda.synchronize()
+        flag = int(ar.error_flag.item())
+        ar.close()
+        results[rank] = ("ok", fused, unfused, fused2, flag, attn.cpu(), w.cpu())
+    except Exception as e:
+        results[rank] = ("error", f"{type(e).__name__}: {e}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_oproj_allreduce_two_ranks():
+    res = _run(_w_fused, 2)
+    ref = sum((res[r][5].float() @ res[r][6].float().t()) for r in range(2))
+    for r in range(2):
+        _, fused, unfused, fused2, flag, _, _ = res[r]
+        assert flag == 0
+        torch.testing.assert_close(fused.float(), ref, atol=3e-2, rtol=1e-2)
+        torch.testing.assert_close(fused.float(), unfused.float(), atol=3e-2, rtol=1e-2)
+        assert torch.equal(fused2, fused[:77])
+    assert torch.equal(res[0][1], res[1][1]) and torch.equal(res[0][3], res[1][3])
