@@ -1,7 +1,8 @@
 """Fused o_proj GEMM + all-reduce (b200kv_oproj_allreduce_f16), single rank:
 the tcgen05 GEMM against an fp32 reference (2e-2 abs / 1e-2 rel on fp16
-outputs of K up to 8192 products) and against cuBLAS; plus the host checks.
-The 2-rank exchange is tested in test_peer_allreduce_gpu.py."""
+outputs of K up to 8192 products) and against cuBLAS, for every split-K
+cluster size (1, 2, 4 CTAs reduced through distributed shared memory); plus
+the host checks.  The 2-rank exchange is tested in test_peer_allreduce_gpu.py."""
 
 import pytest
 import torch
@@ -35,6 +36,52 @@ def test_single_rank_gemm(B, N, K):
     big[:, 32:32 + K] = attn
     out2 = ar.oproj_all_reduce(big[:, 32:32 + K], w)
     assert torch.equal(out2, out)
+    ar.close()
+
+
+@pytest.mark.parametrize("split", [1, 2, 4])
+@pytest.mark.parametrize("B,N,K", [(128, 8192, 4096), (77, 1024, 512), (128, 256, 256), (3, 512, 2048)])
+def test_cluster_split_gemm(split, B, N, K, monkeypatch):
+    from torch_spyre_b200.tp import PeerAllReduce
+
+    attn, w = _case(B, N, K, 7 * B + N + K)
+    ref = attn.float() @ w.float().t()
+    ar = PeerAllReduce(128 * N)
+    monkeypatch.setenv("B200KV_OPROJ_SPLIT", "1")
+    one = ar.oproj_all_reduce(attn, w)
+    monkeypatch.setenv("B200KV_OPROJ_SPLIT", str(split))
+    out = ar.oproj_all_reduce(attn, w)
+    again = ar.oproj_all_reduce(attn, w)
+    torch.cuda.synchronize()
+    assert int(ar.error_flag.item()) == 0
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(out.float(), one.float(), atol=2e-2, rtol=1e-2)
+    assert torch.equal(out, again)  # fixed reduction order: deterministic
+    ar.close()
+
+
+def test_default_split_matches_forced():
+    """The automatic choice (split 2 for K >= 2048 when its clusters fit, else
+    1) gives the bits of the same split asked for explicitly."""
+    import os
+
+    from torch_spyre_b200.tp import PeerAllReduce
+
+    attn, w = _case(128, 8192, 4096, 11)
+    ar = PeerAllReduce(128 * 8192)
+    assert "B200KV_OPROJ_SPLIT" not in os.environ
+    auto = ar.oproj_all_reduce(attn, w)
+    outs = []
+    for split in ("4", "2", "1"):
+        os.environ["B200KV_OPROJ_SPLIT"] = split
+        try:
+            outs.append(ar.oproj_all_reduce(attn, w))
+        except Exception:
+            outs.append(None)
+        finally:
+            del os.environ["B200KV_OPROJ_SPLIT"]
+    torch.cuda.synchronize()
+    assert any(o is not None and torch.equal(auto, o) for o in outs)
     ar.close()
 
 
