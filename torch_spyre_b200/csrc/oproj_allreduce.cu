@@ -49,7 +49,6 @@ constexpr int kOpThreads = 192;
 constexpr int kOpMaxRanks = 8;
 constexpr int kOpPktPerRow = kOpN * 2 / 8;           // 16 packets of 8 data bytes per tile row
 constexpr int kOpPktPerTile = kOpM * kOpPktPerRow;   // 2048
-constexpr int kOpPrefetch = 16;  // default: W slabs prefetched into L2 ahead of the ring
 
 // Shapes of the split-K variant over a cluster of C CTAs.
 template <int C>
@@ -75,7 +74,6 @@ struct OpArgs {
   uint8_t *peers[kOpMaxRanks];
   int rank, world, tiles, batch;
   int kblocks;
-  int prefetch;  // W slabs prefetched into L2 ahead of the ring (0: none)
   __half *out;
   int64_t out_sb;
   int64_t recv1_off, recv2_off, region_bytes, counter_off;
@@ -96,12 +94,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
           smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
-}
-
-// Prefetch of one W box into L2 (no shared memory, no completion to wait on).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(c0), "r"(c1)
-               : "memory");
 }
 
 __device__ __forceinline__ void st_volatile_v4(uint4 *p, uint4 v) {
@@ -216,14 +208,7 @@ __global__ void __launch_bounds__(kOpThreads, 1)
 
   if (warp == 4) {
     if (lane == 0) {  // producer
-      // W streams from HBM and the ring (shared memory) bounds the bytes an SM
-      // keeps in flight; L2 prefetches of the W slabs a.prefetch ahead of the
-      // ring keep DRAM busy without shared memory, so the ring's loads mostly
-      // see L2 latency.
-      const int pf = a.prefetch;
-      for (int i = 0; i < kpc && i < pf; ++i) tma_prefetch_2d(&wmap, (kb0 + i) * kOpK, cn0);
       for (int i = 0; i < kpc; ++i) {
-        if (i + pf < kpc) tma_prefetch_2d(&wmap, (kb0 + i + pf) * kOpK, cn0);
         const int s = i % kStages;
         const uint32_t ph = (i / kStages) & 1u;
         mbar_wait_bounded(&empty[s], ph ^ 1u, a.error_flag);
@@ -582,9 +567,6 @@ extern "C" int b200kv_oproj_allreduce_f16(const void *attn, int64_t attn_stride_
   a.tiles = static_cast<int>(tiles);
   a.batch = static_cast<int>(batch);
   a.kblocks = static_cast<int>(k / kOpK);
-  a.prefetch = kOpPrefetch;
-  if (const char *e = std::getenv("B200KV_OPROJ_PREFETCH")) a.prefetch = std::atoi(e);
-  B200KV_CHECK_ARG(a.prefetch >= 0 && a.prefetch <= 1024, "B200KV_OPROJ_PREFETCH must be in [0, 1024]");
   a.out = static_cast<__half *>(out);
   a.out_sb = out_stride_b;
   peer_regions(capacity_elems, world, &a.recv1_off, &a.recv2_off, &a.region_bytes, &a.counter_off);
