@@ -633,7 +633,11 @@ def run_relayout(args, rank, world, local):
         "config": {"workload": "relayout", "bulk_tokens": T, "num_kv_heads": hkv, "head_dim": D,
                    "append_tokens": n, "l2": f"{2 * bulk / 1e6:.0f} MB per direction > 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_source": kind, "traffic": None,
+                     "frac": round(achieved / peak, 4), "peak_source": kind,
+                     "traffic": (round(ratio * step_bytes) if (ratio := profiled_traffic_ratio(
+                         "relayout_kernels", "relayout")) else None),
+                     "traffic_source": "ncu dram__bytes_read+write / algorithmic of one step "
+                                       "(profiles/relayout_kernels_relayout.md), times this run's bytes",
                      "kernel": "kv_append + relayout_kernel<0> + relayout_kernel<1> (one step)",
                      "algorithmic_bytes_per_launch": step_bytes, "mean_launch_ms": round(launch_ms, 5)},
         "gpu_launches": 3 * steps,
