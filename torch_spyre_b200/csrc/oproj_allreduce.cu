@@ -30,7 +30,9 @@
 //            rank, which polls it into its output.
 // Transfers are the flagged 8-byte packets of peer_allreduce.cu (data + epoch,
 // receiver polls, no fences, no multicast) in the same peer buffers, receive
-// regions and epoch counter, so fused and unfused calls interleave.  All CTAs
+// regions and epoch counter, so fused and unfused calls interleave.  Inside a
+// tile's region packet j of row r sits at j * 128 + r, so a warp's stores and
+// polls cover 512 contiguous bytes, and a row's packets are polled as a batch.  All CTAs
 // are resident at once (checked on the host: N / 64 <= SMs for C = 1, enough
 // co-resident clusters for C > 1), so no CTA waits on one that cannot run.
 // Every mbarrier / packet wait is bounded (2 s); every thread of a cluster
@@ -109,6 +111,37 @@ __device__ __forceinline__ uint4 ld_volatile_v4(const uint4 *p) {
   return v;
 }
 
+// Receives kOpPktHalf packets of one tile row (packet j at p + j * stride;
+// each packet is two 8-byte {data, epoch} words, complete when both carry
+// `epoch`): the loads are issued at once and only the packets not yet complete
+// are polled again, so packets that have arrived cost one memory round trip
+// (polling them one by one would chain a round trip per packet).  Gives up
+// after kWaitLimitNs (sets B200KV_DEVERR_TIMEOUT and `dead`, which also stops
+// the thread's later waits).
+constexpr int kOpPktHalf = kOpPktPerRow / 2;
+__device__ __forceinline__ void recv_packets(const uint4 *p, int stride, uint32_t epoch, uint64_t t0, bool &dead,
+                                             int32_t *err, uint2 (&out)[kOpPktHalf]) {
+  uint4 v[kOpPktHalf];
+#pragma unroll
+  for (int j = 0; j < kOpPktHalf; ++j) v[j] = ld_volatile_v4(p + j * stride);
+  for (uint32_t i = 0; !dead; ++i) {
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < kOpPktHalf; ++j) ok = ok && v[j].y == epoch && v[j].w == epoch;
+    if (ok) break;
+    if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+      dead = true;
+      if (err) atomicOr(err, B200KV_DEVERR_TIMEOUT);
+      break;
+    }
+#pragma unroll
+    for (int j = 0; j < kOpPktHalf; ++j)
+      if (v[j].y != epoch || v[j].w != epoch) v[j] = ld_volatile_v4(p + j * stride);
+  }
+#pragma unroll
+  for (int j = 0; j < kOpPktHalf; ++j) out[j] = make_uint2(v[j].x, v[j].z);
+}
+
 // One warp reads 64 consecutive fp32 columns of its 32 TMEM lanes (lane = row).
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile(
@@ -143,21 +176,6 @@ __device__ __forceinline__ uint32_t mapa_cluster(uint32_t smem_addr, uint32_t ra
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
   asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
-}
-
-// Polls packet p until both words carry `epoch` (bounded; `dead` stops it).
-__device__ __forceinline__ uint2 recv_pkt(const uint4 *p, uint32_t epoch, uint64_t t0, bool &dead, int32_t *err) {
-  uint4 v;
-  for (uint32_t i = 0;; ++i) {
-    v = ld_volatile_v4(p);
-    if ((v.y == epoch && v.w == epoch) || dead) break;
-    if ((i & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
-      dead = true;
-      if (err) atomicOr(err, B200KV_DEVERR_TIMEOUT);
-      break;
-    }
-  }
-  return make_uint2(v.x, v.z);
 }
 
 template <int C>
@@ -321,7 +339,9 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     const int owner = tile / per_owner, local = tile - owner * per_owner;
     const int64_t par_off = int64_t(epoch & 1u) * a.region_bytes;
     const int64_t slot_pk = int64_t(per_owner) * kOpPktPerTile;  // packets per source slot
-    const int64_t pk0 = int64_t(local) * kOpPktPerTile + int64_t(row) * kOpPktPerRow;
+    // packet j of row r of a tile sits at j * 128 + r: the 32 lanes of a warp
+    // (32 consecutive rows) move 512 contiguous bytes per packet index
+    const int64_t pk0 = int64_t(local) * kOpPktPerTile + row;
     __half *orow = a.out + int64_t(row) * a.out_sb + n0;
     const uint64_t t0 = global_timer_ns();
     bool dead = false;
@@ -330,12 +350,15 @@ __global__ void __launch_bounds__(kOpThreads, 1)
         // send the partial row to the owner, then take the sum back
         uint4 *dst = reinterpret_cast<uint4 *>(a.peers[owner] + a.recv1_off + par_off) + int64_t(me) * slot_pk + pk0;
 #pragma unroll
-        for (int j = 0; j < kOpPktPerRow; ++j) st_volatile_v4(dst + j, make_uint4(h[2 * j], epoch, h[2 * j + 1], epoch));
+        for (int j = 0; j < kOpPktPerRow; ++j)
+          st_volatile_v4(dst + j * kOpM, make_uint4(h[2 * j], epoch, h[2 * j + 1], epoch));
         const uint4 *src = reinterpret_cast<const uint4 *>(a.peers[me] + a.recv2_off + par_off) + int64_t(owner) * slot_pk + pk0;
 #pragma unroll
-        for (int j = 0; j < kOpPktPerRow; ++j) {
-          const uint2 v = recv_pkt(src + j, epoch, t0, dead, a.error_flag);
-          *reinterpret_cast<uint2 *>(orow + 4 * j) = v;
+        for (int hf = 0; hf < 2; ++hf) {
+          uint2 got[kOpPktHalf];
+          recv_packets(src + hf * kOpPktHalf * kOpM, kOpM, epoch, t0, dead, a.error_flag, got);
+#pragma unroll
+          for (int j = 0; j < kOpPktHalf; ++j) *reinterpret_cast<uint2 *>(orow + 4 * (hf * kOpPktHalf + j)) = got[j];
         }
       } else {
         // owner: sum the N partial rows in rank order, keep and send the sum
@@ -345,14 +368,20 @@ __global__ void __launch_bounds__(kOpThreads, 1)
         for (int q = 0; q < N; ++q) {
           const uint4 *src = reinterpret_cast<const uint4 *>(a.peers[me] + a.recv1_off + par_off) + int64_t(q) * slot_pk + pk0;
 #pragma unroll
-          for (int j = 0; j < kOpPktPerRow; ++j) {
-            const uint2 v = q == me ? make_uint2(h[2 * j], h[2 * j + 1]) : recv_pkt(src + j, epoch, t0, dead, a.error_flag);
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
-            acc[4 * j] += f0.x;
-            acc[4 * j + 1] += f0.y;
-            acc[4 * j + 2] += f1.x;
-            acc[4 * j + 3] += f1.y;
+          for (int hf = 0; hf < 2; ++hf) {
+            uint2 got[kOpPktHalf];
+            if (q != me) recv_packets(src + hf * kOpPktHalf * kOpM, kOpM, epoch, t0, dead, a.error_flag, got);
+#pragma unroll
+            for (int jj = 0; jj < kOpPktHalf; ++jj) {
+              const int j = hf * kOpPktHalf + jj;
+              const uint2 v = q == me ? make_uint2(h[2 * j], h[2 * j + 1]) : got[jj];
+              const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+              const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+              acc[4 * j] += f0.x;
+              acc[4 * j + 1] += f0.y;
+              acc[4 * j + 2] += f1.x;
+              acc[4 * j + 3] += f1.y;
+            }
           }
         }
         uint32_t s[32];
@@ -368,7 +397,8 @@ __global__ void __launch_bounds__(kOpThreads, 1)
           if (q == me) continue;
           uint4 *dst = reinterpret_cast<uint4 *>(a.peers[q] + a.recv2_off + par_off) + int64_t(me) * slot_pk + pk0;
 #pragma unroll
-          for (int j = 0; j < kOpPktPerRow; ++j) st_volatile_v4(dst + j, make_uint4(s[2 * j], epoch, s[2 * j + 1], epoch));
+          for (int j = 0; j < kOpPktPerRow; ++j)
+            st_volatile_v4(dst + j * kOpM, make_uint4(s[2 * j], epoch, s[2 * j + 1], epoch));
         }
       }
     }
