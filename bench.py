@@ -69,6 +69,8 @@ def parse_args():
                         "o_proj GEMM + all-reduce kernel, or NCCL")
     p.add_argument("--nccl-graph", action="store_true",
                    help="tp70b at N > 1: capture the step, NCCL all-reduce included, in a CUDA graph")
+    p.add_argument("--no-tp", action="store_true",
+                   help="skip the head-sharded tp70b block that every decode workload's line carries")
     return p.parse_args()
 
 
@@ -206,6 +208,42 @@ def cpu_oracle_rate(inp, budget_s: float, max_steps: int | None = None):
             return done / el, done, el
 
 
+# ---------------------------------------------------------------- config ----
+def rotating_sets(kv_bytes_of_set0: float) -> int:
+    """How many rotating input sets keep each step's reads out of L2."""
+    n = max(1, math.ceil(3 * L2_BYTES / kv_bytes_of_set0)) if kv_bytes_of_set0 < 3 * L2_BYTES else 1
+    return min(n, 32)
+
+
+def workload_config(args, cfg, rank, world):
+    """The `config` object of the JSON line, computed from the workload's
+    seeded context lengths alone, so the repo arm and the reference arm print
+    the same dictionary for the same run."""
+    from torch_spyre_b200.workloads import context_lens_for
+
+    tp = cfg.name == "tp70b"
+    hkv = cfg.num_kv_heads // world if tp else cfg.num_kv_heads
+    elt = 1 if args.kv_dtype == "fp8" else 2
+
+    def kv_bytes(i):
+        return sum(context_lens_for(cfg, f"set{i}/rank{rank}")) * hkv * cfg.head_dim * 2 * elt
+
+    n_sets = rotating_sets(kv_bytes(0))
+    kv = statistics.mean(kv_bytes(i) for i in range(n_sets))
+    B = len(context_lens_for(cfg, f"set0/rank{rank}"))
+    ar = tp and world > 1 and args.allreduce in ("peer", "fused")
+    graphed = not (tp and world > 1) or args.nccl_graph or ar
+    return {"workload": args.workload, "description": cfg.description, "batch_per_rank": B,
+            "global_batch": B if tp else B * world, "num_q_heads": cfg.num_q_heads,
+            "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
+            "kv_heads_per_rank": hkv, "kv_dtype": args.kv_dtype,
+            "parallelism": (f"tp{world} (kv-head shards + "
+                            f"{'fused o_proj + peer-memory' if args.allreduce == 'fused' and ar else 'peer-memory' if ar else 'NCCL'}"
+                            " all-reduce)" if tp else f"dp{world} (sequence shards)"),
+            "l2": f"{n_sets} rotating input sets, {kv / 1e6:.1f} MB KV read per step (L2 126 MB)",
+            "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")}
+
+
 # ----------------------------------------------------------------- ours -----
 def build_inputs(cfg, rank, world, n_sets, device, start=0, kv_dtype="fp16"):
     from torch_spyre_b200.workloads import make_decode_inputs, quantize_decode_inputs
@@ -239,8 +277,7 @@ def run_ours(args, rank, world, local):
     # how many rotating input sets keep each step's reads out of L2
     fp8 = args.kv_dtype == "fp8"
     probe = build_inputs(cfg, rank, world, 1, device, kv_dtype=args.kv_dtype)[0]
-    n_sets = max(1, math.ceil(3 * L2_BYTES / probe.kv_bytes)) if probe.kv_bytes < 3 * L2_BYTES else 1
-    n_sets = min(n_sets, 32)
+    n_sets = rotating_sets(probe.kv_bytes)
     sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1, kv_dtype=args.kv_dtype)
     step_bytes = statistics.mean(s.step_bytes for s in sets)
     kv_bytes = statistics.mean(s.kv_bytes for s in sets)
@@ -382,22 +419,22 @@ def run_ours(args, rank, world, local):
                          "paged gather + torch CPU SDPA fp32"
                          + (" over the dequantized (fp16) pools" if fp8 else "")}
 
+    config = workload_config(args, cfg, rank, world)
+    assert config["kv_heads_per_rank"] == sets[0].k_pool.shape[1] and config["batch_per_rank"] == B
+    tp_block = None
+    if not tp and not args.no_tp and args.kv_dtype == "fp16":
+        try:
+            tp_block = run_tp_block(args, rank, world, local, device)
+        except Exception as e:  # the headline line still prints
+            tp_block = {"error": f"{type(e).__name__}: {e}"}
+
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "e4m3 KV pages, f16 q/out (fp32 accumulate)" if fp8 else "f16 (fp32 accumulate)",
         "data": "synthetic (seeded N(0,1) fp16 q/K/V, seeded contexts and block permutations)",
-        "config": {"workload": args.workload, "description": cfg.description, "batch_per_rank": B,
-                   "global_batch": tokens_per_step, "num_q_heads": cfg.num_q_heads,
-                   "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
-                   "kv_heads_per_rank": sets[0].k_pool.shape[1], "kv_dtype": args.kv_dtype,
-                   "parallelism": (f"tp{world} (kv-head shards + "
-                                   f"{'fused o_proj + peer-memory' if fused else 'peer-memory' if ar is not None else 'NCCL'}"
-                                   " all-reduce)" if tp
-                                   else f"dp{world} (sequence shards)"),
-                   "l2": f"{n_sets} rotating input sets, {kv_bytes / 1e6:.1f} MB KV read per step (L2 126 MB)",
-                   "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")},
+        "config": config,
         "kv_gbs": round(kv_bytes / (ms_per_step / 1e3) / 1e9, 1),
         "roofline": roofline,
         "e2e": e2e,
@@ -406,7 +443,10 @@ def run_ours(args, rank, world, local):
         "gpu_launches": steps * (2 if ar is not None else 1),
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
+        "tp": tp_block,
     }
+    if tp_block is not None and "tp_parity_ok" in tp_block:
+        line["tp_parity_ok"] = tp_block["tp_parity_ok"]
     if rank == 0:
         print(json.dumps(line), flush=True)
     if ar is not None:
@@ -563,6 +603,189 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
                         "overlapping the neighbouring steps' compute" if graph_ms is not None
                         else "eager")),
             "eager": {"value": round(tokens / (eager_ms / 1e3), 1), "ms_per_step": round(eager_ms, 5)}}
+
+
+# ------------------------------------------------ tensor-parallel block ----
+TP_STEPS = 300          # timed TP steps per variant (each 60-240 us)
+TP_COMPONENT_REPS = 20  # launches per captured graph when timing one component
+TP_PARITY_CTX = [1000, 64, 3000, 17, 4096, 2000, 5, 777]  # ragged: partial pages, ctx < 64
+TP_ATOL, TP_RTOL = 1e-2, 1e-2  # o_proj output vs the fp32 oracle (fp16 attn, fp16 partials)
+
+
+def _graph_us(fns, stream, world, replays, per_graph):
+    """Device time of one launch of a component: `fns` captured once in a CUDA
+    graph, replayed `replays` times back to back, CUDA events on the launching
+    stream; max over ranks.  Every rank must call this in the same order."""
+    with torch.cuda.stream(stream):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for f in fns:
+                f()
+        for _ in range(3):
+            g.replay()
+        stream.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(replays):
+            g.replay()
+        b.record(stream)
+        stream.synchronize()
+    us = 1e3 * a.elapsed_time(b) / (replays * per_graph)
+    del g
+    return max_over_ranks(us, world)
+
+
+def tp_parity_check(rank, world, device, ar, fused_ok):
+    """Checker, run after the timed region: one small head-sharded step (ragged
+    contexts, partial pages) through each path the block times, against the
+    CPU oracle (the reference's CPU eager decode of all heads, then the full
+    o_proj in fp32).  Returns (ok on every rank, max abs error over ranks)."""
+    from oracle.tp_step import tp_step_cpu
+    from torch_spyre_b200.tp import HeadShard, tp_decode_step
+    from torch_spyre_b200.workloads import DECODE_CONFIGS, make_decode_inputs, seeded_generator
+
+    cfg = DECODE_CONFIGS["tp70b"]
+    full = make_decode_inputs(cfg, ctx=TP_PARITY_CTX, seed_tag="tp-parity")
+    w_o = (torch.randn((cfg.hidden, cfg.num_q_heads * cfg.head_dim), generator=seeded_generator("tp-parity", "w_o"))
+           * 0.02).to(torch.float16)
+    shard = HeadShard(rank, world, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
+    step_args = (shard, shard.shard_q(full.q.to(device)), shard.shard_pool(full.k_pool).to(device),
+                 shard.shard_pool(full.v_pool).to(device), full.block_table.to(device), full.context_lens.to(device),
+                 shard.shard_w_o(w_o).to(device))
+    ys = {}
+    if world == 1:
+        ys["local"] = tp_decode_step(*step_args)
+    else:
+        ys["peer"] = tp_decode_step(*step_args, allreduce=ar).clone()
+        if fused_ok:
+            ys["fused"] = tp_decode_step(*step_args, allreduce=ar, fused_oproj=True).clone()
+        ys["nccl"] = tp_decode_step(*step_args)
+    torch.cuda.synchronize(device)
+    ref = tp_step_cpu(full.q, full.k_pool, full.v_pool, full.block_table, full.context_lens, w_o)
+    ok, err = True, 0.0
+    for y in ys.values():
+        y = y.cpu().float()
+        ok &= bool(torch.allclose(y, ref, atol=TP_ATOL, rtol=TP_RTOL))
+        err = max(err, float((y - ref).abs().max()))
+    if ar is not None:
+        ok &= int(ar.error_flag.item()) == 0
+    flag = -max_over_ranks(-float(ok), world)  # min over ranks
+    return flag == 1.0, max_over_ranks(err, world), sorted(ys)
+
+
+def run_tp_block(args, rank, world, local, device):
+    """BASELINE config 4 at this N: the head-sharded decode step (rank r owns KV
+    heads [r*8/N, (r+1)*8/N), their q heads and pages and W_o's matching input
+    columns; one SUM all-reduce of the fp16 [128, 8192] o_proj partial), strong
+    scaling (global batch 128 at every N).  Times the whole step with the
+    default all-reduce (the peer-memory kernel at N > 1) and with the fused
+    o_proj + all-reduce kernel, and each component alone; then checks one small
+    step against the CPU oracle.  Every rank takes the same steps in the same
+    order."""
+    import torch_spyre_b200 as tsb
+    from torch_spyre_b200.tp import HeadShard, PeerAllReduce, tp_decode_step
+    from torch_spyre_b200.workloads import DECODE_CONFIGS
+
+    cfg = DECODE_CONFIGS["tp70b"]
+    if cfg.num_kv_heads % world:
+        return {"error": f"{world} ranks do not divide {cfg.num_kv_heads} KV heads"}
+    probe = build_inputs(cfg, rank, world, 1, device)[0]
+    n_sets = min(32, max(1, math.ceil(3 * L2_BYTES / probe.kv_bytes)))
+    sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1)
+    B = len(sets[0].ctx)
+    shard = HeadShard(rank, world, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
+    K = len(shard.q_heads) * cfg.head_dim
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + rank)
+    w_o = torch.randn((cfg.hidden, K), generator=g, device=device, dtype=torch.float16) * 0.02
+    # W_o copies that together exceed L2, so the o_proj timed alone streams its
+    # weights from HBM as it does inside the step
+    n_w = min(24, max(1, math.ceil(3 * L2_BYTES / w_o.numel() / 2)))
+    w_rot = [w_o] + [w_o.clone() for _ in range(n_w - 1)]
+    attn = tsb.decode_attention(sets[0].q, sets[0].k_pool, sets[0].v_pool, sets[0].block_table,
+                                sets[0].context_lens).reshape(B, K)
+    ar = PeerAllReduce(B * cfg.hidden, device=device)
+    # the fused kernel needs hidden / (64 N) whole tiles and 128 co-resident CTAs
+    fused_ok = cfg.hidden % (64 * world) == 0 and B <= 128
+    partial = torch.empty((B, cfg.hidden), dtype=torch.float16, device=device)
+    stream = torch.cuda.Stream(device)
+
+    def step(s, fused=False):
+        if world == 1 and not fused:
+            return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o, out=partial)
+        return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
+                              out=partial if fused else None, allreduce=ar, fused_oproj=fused)
+
+    with torch.cuda.stream(stream):
+        for s in sets:
+            step(s)
+            if fused_ok:
+                step(s, fused=True)
+        stream.synchronize()
+    barrier(world)
+    reps = max(1, -(-TP_STEPS // n_sets))
+    res = {"workload": "tp70b", "parallelism": f"tp{world} (kv-head shards)", "global_batch": B,
+           "kv_heads_per_rank": sets[0].k_pool.shape[1], "q_heads_per_rank": len(shard.q_heads),
+           "oproj_shape": [B, cfg.hidden, K], "input_sets": n_sets, "w_o_copies_for_oproj_alone": n_w,
+           "steps": reps * n_sets, "allreduce": "peer-memory kernel" if world > 1 else "none (N = 1)"}
+    with ClockSampler(local if world > 1 else 0) as clk:
+        step_us = _graph_us([lambda s=s: step(s) for s in sets], stream, world, reps, n_sets)
+        fused_us = (_graph_us([lambda s=s: step(s, True) for s in sets], stream, world, reps, n_sets)
+                    if fused_ok else None)
+        dec_us = _graph_us([lambda s=s: tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table,
+                                                             s.context_lens) for s in sets],
+                           stream, world, reps, n_sets)
+        oproj_reps = max(1, TP_COMPONENT_REPS // n_w) * n_w
+        oproj_us = _graph_us([lambda w=w_rot[i % n_w]: torch.matmul(attn, w.t(), out=partial)
+                              for i in range(oproj_reps)], stream, world, 10, oproj_reps)
+        fused_alone_us = (_graph_us([lambda w=w_rot[i % n_w]: ar.oproj_all_reduce(attn, w, out=partial)
+                                     for i in range(oproj_reps)], stream, world, 10, oproj_reps)
+                          if fused_ok else None)
+        ar_us = nccl_us = None
+        if world > 1:
+            buf = ar.buffer((B, cfg.hidden))
+            buf.zero_()
+            ar_us = _graph_us([lambda: ar.all_reduce(buf)] * TP_COMPONENT_REPS, stream, world, 10,
+                              TP_COMPONENT_REPS)
+            import torch.distributed as dist
+
+            nbuf = torch.zeros((B, cfg.hidden), dtype=torch.float16, device=device)
+            with torch.cuda.stream(stream):
+                for _ in range(5):
+                    dist.all_reduce(nbuf)
+                stream.synchronize()
+                barrier(world)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(200):
+                    dist.all_reduce(nbuf)
+                b.record(stream)
+                stream.synchronize()
+            nccl_us = max_over_ranks(1e3 * a.elapsed_time(b) / 200, world)
+    peak, peak_kind = hbm_peak()
+    dec_bytes = statistics.mean(s.step_bytes for s in sets)
+    res.update({
+        "value": round(B / (step_us / 1e6), 1), "unit": "tokens/s", "ms_per_step": round(step_us / 1e3, 5),
+        "value_fused": round(B / (fused_us / 1e6), 1) if fused_us else None,
+        "ms_per_step_fused": round(fused_us / 1e3, 5) if fused_us else None,
+        "decode_us": round(dec_us, 2),
+        "decode_frac": round(dec_bytes / (dec_us / 1e6) / 1e9 / peak, 4), "decode_peak_gbs": peak,
+        "decode_peak_source": peak_kind, "decode_bytes_per_launch": int(dec_bytes),
+        "oproj_us": round(oproj_us, 2), "oproj": "cuBLAS (torch.matmul) into the peer buffer",
+        "oproj_fused_allreduce_us": round(fused_alone_us, 2) if fused_alone_us else None,
+        "allreduce_us": round(ar_us, 2) if ar_us else None,
+        "allreduce_nccl_us": round(nccl_us, 2) if nccl_us else None,
+        "gpu_launches": res["steps"] * (2 if world > 1 else 1),
+        "clocks": clk.summary(),
+    })
+    ok, err, paths = tp_parity_check(rank, world, device, ar if world > 1 else None, fused_ok)
+    res.update({"tp_parity_ok": ok, "tp_parity_max_abs_err": round(err, 6), "tp_parity_paths": paths,
+                "tp_parity_case": f"B={len(TP_PARITY_CTX)} ctx {TP_PARITY_CTX}, all heads, hidden {cfg.hidden}, "
+                                  f"vs CPU oracle (decode x W_o in fp32), atol {TP_ATOL} rtol {TP_RTOL}"})
+    del w_rot
+    ar.close()
+    return res
 
 
 # --------------------------------------------------------------- relayout ----
@@ -724,7 +947,7 @@ def run_reference(args, rank, world):
         "steps": steps, "warmup": warmup, "ms_per_step": round(1e3 * total / steps, 4), "higher_is_better": True,
         "scaling": "strong" if cfg.name == "tp70b" else "weak", "vs_baseline": None, "dtype": "f32 (CPU SDPA)",
         "data": "synthetic (seeded N(0,1) fp16 q/K/V)",
-        "config": {"workload": args.workload, "description": cfg.description},
+        "config": workload_config(args, cfg, 0, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": torch.get_num_threads(),
                          "kind": "port", "sample": f"{per_step} sequence(s) per step of the {args.workload} batch, "
                                                    "paged gather + torch CPU SDPA (reference CPU eager path)"},

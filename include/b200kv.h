@@ -222,10 +222,13 @@ B200KV_API int b200kv_decode_attention_append_f16(
  * of b200kv_decode_attention_f16.  Same arguments minus num_splits and the
  * workspace; the caller still passes every input and output.  The split-KV
  * partials go to a 16 MiB scratch array the library keeps on each device that
- * loads it (until process exit); batch * num_kv_heads must be <= 16384 and the
- * partials must fit in the scratch (else B200KV_ERR_UNSUPPORTED).  The first
- * call on a device looks up the scratch address, so make it before any stream
- * capture.  Calls share the scratch: calls that overlap on the GPU race. */
+ * loads it (until process exit).  Limit, else B200KV_ERR_UNSUPPORTED before any
+ * launch: pairs = batch * num_kv_heads <= 16384 and
+ * 64 KiB + (pairs + SMs) * G * 520 B <= 16 MiB (G = num_q_heads / num_kv_heads,
+ * 148 SMs on B200): about 15900 pairs at G = 2, 7880 at G = 4, 3860 at G = 8.
+ * The first call on a device looks up the scratch address, so make it before
+ * any stream capture (a failed lookup is retried by the next call).  Calls
+ * share the scratch: calls that overlap on the GPU race. */
 B200KV_API int b200kv_decode_attention_f16_noalloc(
     const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
     const void *v_pool, const int32_t *block_table, int64_t block_table_stride,

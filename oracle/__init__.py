@@ -1,7 +1,8 @@
 """CPU oracle for the paged decode path -- TEST INFRASTRUCTURE ONLY.
 
-Only `tests/`, `__graft_entry__.smoke()` and the CPU-baseline leg of `bench.py`
-may import this package, and only as the checker (or the timed CPU baseline).
+Only `tests/`, `__graft_entry__.smoke()` and `bench.py` (its CPU-baseline leg,
+the reference arm, and the TP parity check run after the timed region) may
+import this package, and only as the checker (or the timed CPU baseline).
 The product (`torch_spyre_b200`) never imports it and has no CPU fallback.
 
 Contents
@@ -19,6 +20,9 @@ Contents
   kv_relayout      numpy restatement of the KV append (overwrite_cpu,
                    torch_spyre/_inductor/customops.py:298-308; index_copy_) and
                    of the row-major <-> paged stick relayout, bit-exact.
+  tp_step          the head-sharded TP step: decode of all heads, then the
+                   full o_proj in fp32 (= the SUM all-reduce of the per-rank
+                   partials, spyre_ccl.cpp:470-494).
 
 Parity pinning: the layout restatement is checked against the reference's
 golden layout vectors (tests/tensor/test_tensor_layout.py:39-104, 193-280); the

@@ -4,10 +4,13 @@ Inputs are the reference's own decode-test tensors: `cached_randn` of
 tests/inductor/utils_inductor.py:27-50 with the shapes and differentiation tags
 of the `mha_decode` / `gqa_decode` param sets (tests/inductor/
 test_inductor_ops.py:2651-2678) and of test_index_copy_inplace_{prefill,decode}
-(5688-5740).  When the reference tree is present its `cached_randn` is imported
-(the spyre device name is registered first so the module imports without the
-Spyre runtime) and checked against this repo's `seeded_randn`; otherwise
-`seeded_randn` alone is used.
+(5688-5740).  When a checkout of the reference is given (``--reference DIR``
+or the environment variable TORCH_SPYRE_REFERENCE, the root of a torch-spyre
+tree) its `cached_randn` is imported (the spyre device name is registered
+first so the module imports without the Spyre runtime) and checked against
+this repo's `seeded_randn`; otherwise `seeded_randn` alone is used.
+
+Usage: python tests/golden/make_golden.py [--reference DIR]
 
 Outputs are what the reference's harness treats as the truth: the test
 function run eagerly on CPU tensors (compare_with_cpu,
@@ -42,11 +45,25 @@ sys.path.insert(0, str(REPO))
 
 from torch_spyre_b200.workloads import seeded_randn  # noqa: E402
 
-REF_TESTS = Path("/root/reference/tests/inductor")
+def reference_tests_dir():
+    """tests/inductor of the reference checkout named on the command line or in
+    TORCH_SPYRE_REFERENCE (None if neither names an existing tree)."""
+    import argparse
+    import os
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("TORCH_SPYRE_REFERENCE"),
+                    help="root of a torch-spyre checkout whose cached_randn pins the inputs")
+    root = ap.parse_args().reference
+    if not root:
+        return None
+    d = Path(root) / "tests" / "inductor"
+    return d if d.exists() else None
 
 
 def reference_randn():
-    if not REF_TESTS.exists():
+    REF_TESTS = reference_tests_dir()
+    if REF_TESTS is None:
         return None
     try:
         torch.utils.rename_privateuse1_backend("spyre")

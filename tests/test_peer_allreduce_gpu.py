@@ -2,7 +2,9 @@
 
 * sums are bit-exact against fp32 accumulation in rank order rounded once;
 * repeated calls and CUDA-graph replays (the epoch lives in device memory);
-* the TP decode step through it equals the NCCL path;
+* the fused o_proj + all-reduce kernel against the fp32 sum of the ranks'
+  o_proj products (the TP decode step through every all-reduce path is checked
+  against the CPU oracle in test_tp_gpu.py);
 * a peer that never joins ends the wait after its 2 s bound with
   B200KV_DEVERR_TIMEOUT, and the context stays usable.
 Ranks run as spawned processes (NVLS off; the kernel uses plain peer stores).
@@ -107,8 +109,10 @@ def _run(target, world=2, timeout=300):
     return res
 
 
-def test_peer_allreduce_sums_bit_exact():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_allreduce_sums_bit_exact(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     res = _run(_w_sums, world)
     sizes = [128 * 8192, 16 * 8192, 8 * world, 4096 * world]
     for r in range(world):
@@ -119,42 +123,6 @@ def test_peer_allreduce_sums_bit_exact():
         for k in range(3):
             exp = _expected(_partials(world, 64 * 8192, 200 + k))
             assert torch.equal(graphed[k].view(torch.int16), exp.view(torch.int16))
-
-
-def _w_tp(rank, world, port, results):
-    dist = _init(rank, world, port)
-    from test_tp_gpu import _inputs
-
-    from torch_spyre_b200.tp import HeadShard, PeerAllReduce, tp_decode_step
-
-    try:
-        cfg, inp, w_o = _inputs()
-        shard = HeadShard(rank, world, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
-        dev = torch.device("cuda", rank)
-        args = (shard, shard.shard_q(inp.q.to(dev)), shard.shard_pool(inp.k_pool).to(dev),
-                shard.shard_pool(inp.v_pool).to(dev), inp.block_table.to(dev), inp.context_lens.to(dev),
-                shard.shard_w_o(w_o).to(dev))
-        y_nccl = tp_decode_step(*args).cpu()
-        ar = PeerAllReduce(len(inp.ctx) * w_o.shape[0])
-        y_peer = tp_decode_step(*args, allreduce=ar).cpu().clone()
-        torch.cuda.synchronize()
-        flag = int(ar.error_flag.item())
-        ar.close()
-        results[rank] = ("ok", y_nccl, y_peer, flag)
-    except Exception as e:
-        results[rank] = ("error", f"{type(e).__name__}: {e}")
-    finally:
-        dist.destroy_process_group()
-
-
-def test_tp_step_peer_allreduce_matches_nccl():
-    res = _run(_w_tp, 2)
-    for r in range(2):
-        _, y_nccl, y_peer, flag = res[r]
-        assert flag == 0
-        # NCCL adds two fp16 partials in fp16, the peer kernel in fp32: one rounding apart
-        torch.testing.assert_close(y_peer.float(), y_nccl.float(), atol=2e-3, rtol=2e-3)
-    assert torch.equal(res[0][2], res[1][2])
 
 
 def _w_timeout(rank, world, port, results):

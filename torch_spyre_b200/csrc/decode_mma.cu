@@ -19,15 +19,20 @@
 //             (K, V; 16 KiB each, 128-byte swizzle, L2 evict-first) and, with
 //             the first page of a piece, one bulk copy per q row, into an
 //             NST-stage ring with "full"/"empty" mbarriers;
-//   consumers warp w owns tokens [16w, 16w + 16) of every page and keeps its
-//             own online-softmax state, so no CTA barrier is taken per page:
-//               S^T[16 t x 8 h] = K[16 t x 128 d] . Q^T   (8 mma, ldmatrix)
-//               mask t >= ctx, exp2-domain online softmax (shuffles over t)
-//               P^T fragment from S^T by movmatrix.trans
-//               O^T[128 d x 8 h] += V^T[128 d x 16 t] . P^T (8 mma, ldmatrix.trans)
+//   consumers take the ring's stages in turn: warp w processes the whole
+//             pages of stages w, w + 4, w + 8, ... (and only reads the
+//             descriptors of the others), each with its own online-softmax
+//             state per piece, so no CTA barrier is taken per page.  Per page:
+//               S^T[64 t x 8 h] = K[64 t x 128 d] . Q^T   (four 16-token MMA
+//                                 chains, ldmatrix at precomputed offsets)
+//               mask t >= ctx, one exp2-domain online-softmax update for the
+//               page (quad shuffles)
+//               P^T fragments from S^T by movmatrix.trans
+//               O^T[128 d x 8 h] += V^T[128 d x 64 t] . P^T (ldmatrix.trans,
+//                                 eight dim tiles x four token steps)
 //             then one arrive on the stage's empty barrier; at the end of a
-//             piece each warp drops its state into one of two piece buffers
-//             and goes on with the next page;
+//             piece the warp drops its state into one of two piece buffers
+//             and goes on with its next page;
 //   epilogue  merges the 4 warps' states of a finished piece, writes the fp16
 //             output (unsplit pair) or the fp32 partial, takes the pair's
 //             completion ticket and, holding the last one, merges the pair's

@@ -11,14 +11,23 @@
 //
 // The scratch is a file-scope __device__ array, so every GPU that loads the
 // library holds it (kScratchBytes) until the process exits.  Its device
-// address is looked up once per device with cudaGetSymbolAddress (host code
-// may not use the array's name as a device pointer); the first call on each
-// device does that lookup, so make that first call before any stream capture.
+// address is looked up with cudaGetSymbolAddress (host code may not use the
+// array's name as a device pointer) by the first call on each device, with
+// that device current, so make that first call before any stream capture.
+// Only a successful lookup is kept: a call whose lookup failed returns the
+// CUDA error and the next call on that device tries again.
 // All calls on a device share the array and it keeps the last call's data:
 // each call clears the completion counters it uses, and calls that overlap on
 // the GPU (different streams, no ordering between them) race on the scratch.
-// The caller still passes all inputs and outputs.  Sizes whose scratch need
-// exceeds kScratchBytes are rejected with B200KV_ERR_UNSUPPORTED.
+// The caller still passes all inputs and outputs.
+// Limit: batch * num_kv_heads <= 16384 and
+//   64 KiB + (batch * num_kv_heads + SMs) * G * 520 bytes <= 16 MiB
+// (G = num_q_heads / num_kv_heads, SMs = 148 on B200; 520 = 128 fp32 outputs
+// plus one (max, sum) pair per query head, the 256-byte alignment of the
+// partial region aside): at most about 15900 (sequence, KV head) pairs at
+// G = 2, 7880 at G = 4, 3860 at G = 8.  Larger sizes are rejected with
+// B200KV_ERR_UNSUPPORTED before anything is launched.
+#include <atomic>
 #include <cmath>
 #include <mutex>
 
@@ -34,21 +43,27 @@ constexpr int64_t kCounterBytes = kNoAllocMaxPairs * 4;
 static __device__ __align__(256) uint8_t g_decode_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-uint8_t *g_scratch_ptr[kMaxDevices] = {nullptr};
-std::once_flag g_scratch_once[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices] = {cudaSuccess};
+std::atomic<uint8_t *> g_scratch_ptr[kMaxDevices];
+std::mutex g_scratch_mutex;
 
-// Device address of the scratch array on the current device (looked up once).
+// Device address of the scratch array on the current device `dev`.  A
+// successful lookup is cached; a failed one is not, so a later call retries.
 int scratch_address(int dev, uint8_t **out) {
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(B200KV_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-  std::call_once(g_scratch_once[dev], [dev] {
-    void *p = nullptr;
-    g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (g_scratch_err[dev] == cudaSuccess) g_scratch_ptr[dev] = static_cast<uint8_t *>(p);
-  });
-  if (g_scratch_err[dev] != cudaSuccess) return cuda_status(g_scratch_err[dev], "cudaGetSymbolAddress");
-  *out = g_scratch_ptr[dev];
+  uint8_t *p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      void *addr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&addr, g_decode_scratch);
+      if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress");
+      p = static_cast<uint8_t *>(addr);
+      g_scratch_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
   return B200KV_OK;
 }
 
