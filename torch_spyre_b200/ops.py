@@ -477,6 +477,91 @@ def merge_attention_states(outs, lses):
 
 
 # ------------------------------------------------------------ SDPA adapter --
+def _sdpa_decode_shapes(query, key, value, enable_gqa):
+    if query.dim() != 4 or key.dim() != 4 or value.dim() != 4 or query.shape[2] != 1:
+        raise ValueError("decode SDPA takes query [B, Hq, 1, D] and key / value [B, Hkv, S, D]")
+    B, Hq, _, D = query.shape
+    Hkv, S = key.shape[1], key.shape[2]
+    if key.shape != value.shape or key.shape[0] != B or key.shape[3] != D:
+        raise ValueError(f"key {tuple(key.shape)} / value {tuple(value.shape)} do not match query {tuple(query.shape)}")
+    if Hq != Hkv and not enable_gqa:
+        raise ValueError("Hq != Hkv requires enable_gqa=True")
+    return B, Hq, Hkv, S, D
+
+
+@torch.library.custom_op("b200kv::sdpa_decode", mutates_args=(), device_types="cuda")
+def _sdpa_decode_op(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, scale: Optional[float],
+                    enable_gqa: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Decode SDPA over dense K/V in a fixed number of launches whatever the
+    batch: the K and V rows of every sequence are written into stick pages by
+    one append launch (sequence b owns pages [b * nblk, (b + 1) * nblk), token
+    s goes to slot b * nblk * 64 + s), then the paged decode kernel runs."""
+    _require_cuda(query, key, value)
+    B, Hq, Hkv, S, D = _sdpa_decode_shapes(query, key, value, enable_gqa)
+    nblk = max(1, -(-S // PAGE_TOKENS))
+    k_pool = torch.empty((B * nblk, Hkv, D // 64, PAGE_TOKENS, 64), dtype=torch.float16, device=query.device)
+    v_pool = torch.empty_like(k_pool)
+    block_table = torch.arange(B * nblk, dtype=torch.int32, device=query.device).view(B, nblk)
+    if B * S > 0:
+        # token-major rows [B * S, Hkv, D] (one copy each when key / value are head-major)
+        rows_k = key.transpose(1, 2).reshape(B * S, Hkv, D)
+        rows_v = value.transpose(1, 2).reshape(B * S, Hkv, D)
+        seq = torch.arange(B, dtype=torch.int64, device=query.device).unsqueeze(1) * (nblk * PAGE_TOKENS)
+        slots = (seq + torch.arange(S, dtype=torch.int64, device=query.device)).reshape(-1)
+        kv_append(rows_k, rows_v, k_pool, v_pool, slots)
+    ctx = torch.full((B,), S, dtype=torch.int32, device=query.device)
+    out, lse = decode_attention(query[:, :, 0, :], k_pool, v_pool, block_table, ctx, scale=scale, return_lse=True)
+    # [B, Hq, D] -> [B, 1, Hq, D] memory order, viewed as [B, Hq, 1, D]
+    return out.unsqueeze(1).transpose(1, 2), lse
+
+
+@_sdpa_decode_op.register_fake
+def _(query, key, value, scale, enable_gqa):
+    B, Hq, _, S, D = _sdpa_decode_shapes(query, key, value, enable_gqa)
+    out = query.new_empty((B, 1, Hq, D)).transpose(1, 2)
+    return out, query.new_empty((B, Hq), dtype=torch.float32)
+
+
+def sdpa_decode(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    scale: Optional[float] = None,
+    enable_gqa: bool = False,
+) -> torch.Tensor:
+    """Decode SDPA with the signature of F.scaled_dot_product_attention
+    (``torch.ops.b200kv.sdpa_decode``, traceable by torch.compile).
+
+    query [B, Hq, 1, D]; key/value dense [B, Hkv, S, D] fp16.  The dense K/V are
+    written into stick pages on the device (identity block table) and the
+    paged decode kernel runs: a constant number of launches for any B.  The
+    result has shape [B, Hq, 1, D] and the memory order [B, 1, Hq, D], like the
+    reference decomposition's output (torch_spyre/_inductor/decompositions.py:
+    592-600).
+    """
+    return torch.ops.b200kv.sdpa_decode(query, key, value, scale, bool(enable_gqa))[0]
+
+
+def _overrideable_tuple(query, key, value, scale, enable_gqa):
+    B, Hq = query.shape[0], query.shape[1]
+    out, lse = torch.ops.b200kv.sdpa_decode(query, key, value, scale, enable_gqa)
+    seed = torch.empty((1,), dtype=torch.float16, device=query.device)
+    offset = torch.empty((1,), dtype=torch.float16, device=query.device)
+    empty = query.new_empty((0,))
+    return out, lse.view(B, Hq, 1), empty, empty, 1, key.shape[2], seed, offset, empty
+
+
+def _check_overrideable_args(query, key, attn_bias, dropout_p, is_causal):
+    if dropout_p > 0.0:
+        raise NotImplementedError("attention dropout is not implemented (as in the reference)")
+    if attn_bias is not None:
+        raise NotImplementedError("an attention bias is not supported by the paged decode path")
+    if query.dim() != 4 or query.shape[2] != 1:
+        raise NotImplementedError("only the decode case (one query position) is implemented")
+    if is_causal and key.shape[2] != 1:
+        raise NotImplementedError("is_causal with one query position masks every key but the first")
+
+
 def scaled_dot_product_fused_attention_overrideable(
     query: torch.Tensor,
     key: torch.Tensor,
@@ -496,55 +581,80 @@ def scaled_dot_product_fused_attention_overrideable(
     must be 1; dropout, an attention bias and a causal mask (which for one
     query position would keep only key 0) are rejected.
     """
-    if dropout_p > 0.0:
-        raise NotImplementedError("attention dropout is not implemented (as in the reference)")
-    if attn_bias is not None:
-        raise NotImplementedError("an attention bias is not supported by the paged decode path")
-    if query.dim() != 4 or query.shape[2] != 1:
-        raise NotImplementedError("only the decode case (one query position) is implemented")
-    if is_causal and key.shape[2] != 1:
-        raise NotImplementedError("is_causal with one query position masks every key but the first")
-    B, Hq, _, D = query.shape
-    Hkv, S = key.shape[1], key.shape[2]
-    out, lse = _sdpa_decode_with_lse(query, key, value, scale, Hq != Hkv)
-    seed = torch.empty((1,), dtype=torch.float16, device=query.device)
-    offset = torch.empty((1,), dtype=torch.float16, device=query.device)
-    return out, lse.view(B, Hq, 1), None, None, 1, S, seed, offset, None
+    _check_overrideable_args(query, key, attn_bias, dropout_p, is_causal)
+    r = _overrideable_tuple(query, key, value, scale, query.shape[1] != key.shape[1])
+    return r[0], r[1], None, None, r[4], r[5], r[6], r[7], None
 
 
-def _sdpa_decode_with_lse(query, key, value, scale, enable_gqa):
-    B, Hq, _, D = query.shape
-    Hkv, S = key.shape[1], key.shape[2]
-    if Hq != Hkv and not enable_gqa:
-        raise ValueError("Hq != Hkv requires enable_gqa=True")
-    nblk = max(1, -(-S // PAGE_TOKENS))
-    k_pool = torch.empty((B * nblk, Hkv, D // 64, PAGE_TOKENS, 64), dtype=torch.float16, device=query.device)
-    v_pool = torch.empty_like(k_pool)
-    block_table = torch.arange(B * nblk, dtype=torch.int32, device=query.device).view(B, nblk)
-    for b in range(B):
-        ids = block_table[b]
-        kv_relayout(key[b].transpose(0, 1).contiguous(), k_pool, ids)
-        kv_relayout(value[b].transpose(0, 1).contiguous(), v_pool, ids)
-    ctx = torch.full((B,), S, dtype=torch.int32, device=query.device)
-    out, lse = decode_attention(query[:, :, 0, :], k_pool, v_pool, block_table, ctx, scale=scale, return_lse=True)
-    # [B, Hq, D] -> [B, 1, Hq, D] memory order, viewed as [B, Hq, 1, D]
-    return out.unsqueeze(1).transpose(1, 2), lse
+# ------------------------------------------------------- SDPA dispatch route --
+_aten_impl: Optional[torch.library.Library] = None
 
-def sdpa_decode(
-    query: torch.Tensor,
-    key: torch.Tensor,
-    value: torch.Tensor,
-    scale: Optional[float] = None,
-    enable_gqa: bool = False,
-) -> torch.Tensor:
-    """Decode SDPA with the signature of F.scaled_dot_product_attention.
 
-    query [B, Hq, 1, D]; key/value dense [B, Hkv, S, D] fp16.  The dense K/V are
-    relaid into stick pages on the device (identity block table) and the paged
-    decode kernel runs.  The result has shape [B, Hq, 1, D] and the memory order
-    [B, 1, Hq, D], like the reference decomposition's output
-    (torch_spyre/_inductor/decompositions.py:592-600).
+def _aten_overrideable_cuda(query, key, value, attn_bias=None, dropout_p=0.0, is_causal=False,
+                            return_debug_mask=False, *, scale=None):
+    _check_overrideable_args(query, key, attn_bias, dropout_p, is_causal)
+    return _overrideable_tuple(query, key, value, scale, query.shape[1] != key.shape[1])
+
+
+def register_sdpa_overrideable() -> None:
+    """Registers this package's decode SDPA as the CUDA kernel of the ATen op
+    the reference implements for its device,
+    ``aten::_scaled_dot_product_fused_attention_overrideable``
+    (torch_spyre/_inductor/decompositions.py:523-611).  Idempotent.  CUDA
+    itself never selects that op, so nothing else changes until a caller
+    calls it or enters :class:`SdpaDecodeMode`."""
+    global _aten_impl
+    if _aten_impl is None:
+        lib = torch.library.Library("aten", "IMPL")
+        lib.impl("_scaled_dot_product_fused_attention_overrideable", _aten_overrideable_cuda, "CUDA")
+        _aten_impl = lib
+
+
+def sdpa_decode_eligible(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False,
+                         enable_gqa=False) -> bool:
+    """Whether F.scaled_dot_product_attention with these arguments is a decode
+    step the paged kernel computes: CUDA fp16, one query position, head_dim
+    128, GQA group 1 / 2 / 4 / 8, no mask, dropout or causal mask."""
+    if not all(isinstance(t, torch.Tensor) for t in (query, key, value)):
+        return False
+    if query.device.type != "cuda" or any(t.dtype != torch.float16 for t in (query, key, value)):
+        return False
+    if query.dim() != 4 or key.dim() != 4 or value.dim() != 4 or query.shape[2] != 1 or query.shape[3] != HEAD_DIM:
+        return False
+    if key.shape != value.shape or key.shape[0] != query.shape[0] or key.shape[3] != HEAD_DIM:
+        return False
+    hq, hkv = query.shape[1], key.shape[1]
+    if hq % hkv or hq // hkv not in (1, 2, 4, 8) or (hq != hkv and not enable_gqa):
+        return False
+    return attn_mask is None and not dropout_p and not (is_causal and key.shape[2] != 1)
+
+
+class SdpaDecodeMode(torch.overrides.TorchFunctionMode):
+    """Routes decode-shaped ``F.scaled_dot_product_attention`` calls to
+    ``aten::_scaled_dot_product_fused_attention_overrideable`` (this package's
+    CUDA kernel) and leaves every other call to torch -- what the reference's
+    ``_fused_sdp_choice`` does for its device by forcing the overrideable
+    backend (torch_spyre/csrc/attn_utils.cpp:22-37).  Install it around the
+    code that holds the SDPA call site (e.g. an HF model's decode step)::
+
+        with tsb.ops.SdpaDecodeMode():
+            logits = model(input_ids, past_key_values=cache).logits
     """
-    if query.dim() != 4 or query.shape[2] != 1:
-        raise ValueError("sdpa_decode handles one query position: query must be [B, Hq, 1, D]")
-    return _sdpa_decode_with_lse(query, key, value, scale, enable_gqa)[0]
+
+    def __enter__(self):
+        register_sdpa_overrideable()
+        return super().__enter__()
+
+    def __torch_function__(self, func, types, args=(), kwargs=None):
+        kwargs = kwargs or {}
+        if func is torch.nn.functional.scaled_dot_product_attention:
+            names = ("query", "key", "value", "attn_mask", "dropout_p", "is_causal", "scale", "enable_gqa")
+            bound = dict(zip(names, args))
+            bound.update(kwargs)
+            if sdpa_decode_eligible(bound.get("query"), bound.get("key"), bound.get("value"),
+                                    bound.get("attn_mask"), bound.get("dropout_p", 0.0),
+                                    bound.get("is_causal", False), bound.get("enable_gqa", False)):
+                return torch.ops.aten._scaled_dot_product_fused_attention_overrideable(
+                    bound["query"], bound["key"], bound["value"], None, 0.0, bool(bound.get("is_causal", False)),
+                    False, scale=bound.get("scale"))[0]
+        return func(*args, **kwargs)
