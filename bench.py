@@ -241,7 +241,8 @@ def workload_config(args, cfg, rank, world):
                             f"{'fused o_proj + peer-memory' if args.allreduce == 'fused' and ar else 'peer-memory' if ar else 'NCCL'}"
                             " all-reduce)" if tp else f"dp{world} (sequence shards)"),
             "l2": f"{n_sets} rotating input sets, {kv / 1e6:.1f} MB KV read per step (L2 126 MB)",
-            "graphs": (f"{n_sets} steps per graph replay" if graphed else "eager (NCCL step)")}
+            "graphs": (f"up to {max(1, 16 // n_sets) * n_sets} steps per graph replay" if graphed
+                       else "eager (NCCL step)")}
 
 
 # ----------------------------------------------------------------- ours -----
@@ -323,36 +324,49 @@ def run_ours(args, rank, world, local):
                 f()
         return g
 
-    # Steps replay from CUDA graphs: one graph holding one step per rotating
-    # input set (so consecutive steps run back to back without a graph launch
-    # in between) plus one single-step graph per set for a remainder.
+    # Steps replay from CUDA graphs, as a serving loop replays its captured
+    # decode steps: one graph holding `rounds` passes over the rotating input
+    # sets (up to 16 steps back to back with no graph launch in between), one
+    # holding one pass, and one single-step graph per set for a remainder.
     graphed = not (tp and world > 1) or args.nccl_graph or ar is not None
+    rounds = max(1, 16 // n_sets)
     with torch.cuda.stream(stream):
         for s in sets:  # warm the op once per set before capture
             step(s)
         stream.synchronize()
-        dec_multi = capture([lambda s=s: decode_only(s) for s in sets])
+        dec_multi = (capture([lambda s=s: decode_only(s) for s in sets] * rounds),
+                     capture([lambda s=s: decode_only(s) for s in sets]))
         dec_single = [capture([lambda s=s: decode_only(s)]) for s in sets]
         if graphed and tp:
-            step_multi = capture([lambda s=s: step(s) for s in sets])
+            step_multi = (capture([lambda s=s: step(s) for s in sets] * rounds),
+                          capture([lambda s=s: step(s) for s in sets]))
             step_single = [capture([lambda s=s: step(s)]) for s in sets]
         elif graphed:
             step_multi, step_single = dec_multi, dec_single
+        # a graph's first replay uploads it: replay each once before any timing
+        for g in [*dec_multi, *dec_single, *((*step_multi, *step_single) if graphed and tp else ())]:
+            g.replay()
+        stream.synchronize()
 
     def run_steps(multi, single, count, eager=None, events=None):
         """Runs `count` steps; returns per-launch durations if events are kept."""
         i, spans = 0, []
         while i < count:
-            n = n_sets if count - i >= n_sets and (multi is not None) else 1
+            if eager is not None:
+                n = 1
+            elif multi is not None and count - i >= rounds * n_sets:
+                n, g = rounds * n_sets, multi[0]
+            elif multi is not None and count - i >= n_sets:
+                n, g = n_sets, multi[1]
+            else:
+                n, g = 1, single[i % n_sets]
             if events is not None:
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
             if eager is not None:
                 eager(sets[i % n_sets])
-            elif n == n_sets:
-                multi.replay()
             else:
-                single[i % n_sets].replay()
+                g.replay()
             if events is not None:
                 b.record(stream)
                 spans.append((a, b, n))
@@ -607,15 +621,19 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
 
 # ------------------------------------------------ tensor-parallel block ----
 TP_STEPS = 300          # timed TP steps per variant (each 60-240 us)
-TP_COMPONENT_REPS = 20  # launches per captured graph when timing one component
+TP_COMPONENT_LAUNCHES = 200  # launches timed per component
 TP_PARITY_CTX = [1000, 64, 3000, 17, 4096, 2000, 5, 777]  # ragged: partial pages, ctx < 64
 TP_ATOL, TP_RTOL = 1e-2, 1e-2  # o_proj output vs the fp32 oracle (fp16 attn, fp16 partials)
 
 
-def _graph_us(fns, stream, world, replays, per_graph):
-    """Device time of one launch of a component: `fns` captured once in a CUDA
-    graph, replayed `replays` times back to back, CUDA events on the launching
-    stream; max over ranks.  Every rank must call this in the same order."""
+def _graph_us(fns, stream, world, launches):
+    """Device time of one launch of a component: `fns` (repeated to at least
+    16 launches) captured once in a CUDA graph, replayed back to back until
+    about `launches` launches ran, CUDA events on the launching stream; max
+    over ranks.  Every rank must call this in the same order."""
+    fns = list(fns) * max(1, -(-16 // len(fns)))
+    per_graph = len(fns)
+    replays = max(1, -(-launches // per_graph))
     with torch.cuda.stream(stream):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -730,24 +748,22 @@ def run_tp_block(args, rank, world, local, device):
            "oproj_shape": [B, cfg.hidden, K], "input_sets": n_sets, "w_o_copies_for_oproj_alone": n_w,
            "steps": reps * n_sets, "allreduce": "peer-memory kernel" if world > 1 else "none (N = 1)"}
     with ClockSampler(local if world > 1 else 0) as clk:
-        step_us = _graph_us([lambda s=s: step(s) for s in sets], stream, world, reps, n_sets)
-        fused_us = (_graph_us([lambda s=s: step(s, True) for s in sets], stream, world, reps, n_sets)
+        n_steps = reps * n_sets
+        step_us = _graph_us([lambda s=s: step(s) for s in sets], stream, world, n_steps)
+        fused_us = (_graph_us([lambda s=s: step(s, True) for s in sets], stream, world, n_steps)
                     if fused_ok else None)
         dec_us = _graph_us([lambda s=s: tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table,
                                                              s.context_lens) for s in sets],
-                           stream, world, reps, n_sets)
-        oproj_reps = max(1, TP_COMPONENT_REPS // n_w) * n_w
-        oproj_us = _graph_us([lambda w=w_rot[i % n_w]: torch.matmul(attn, w.t(), out=partial)
-                              for i in range(oproj_reps)], stream, world, 10, oproj_reps)
-        fused_alone_us = (_graph_us([lambda w=w_rot[i % n_w]: ar.oproj_all_reduce(attn, w, out=partial)
-                                     for i in range(oproj_reps)], stream, world, 10, oproj_reps)
-                          if fused_ok else None)
+                           stream, world, n_steps)
+        oproj_us = _graph_us([lambda w=w: torch.matmul(attn, w.t(), out=partial) for w in w_rot],
+                             stream, world, TP_COMPONENT_LAUNCHES)
+        fused_alone_us = (_graph_us([lambda w=w: ar.oproj_all_reduce(attn, w, out=partial) for w in w_rot],
+                                    stream, world, TP_COMPONENT_LAUNCHES) if fused_ok else None)
         ar_us = nccl_us = None
         if world > 1:
             buf = ar.buffer((B, cfg.hidden))
             buf.zero_()
-            ar_us = _graph_us([lambda: ar.all_reduce(buf)] * TP_COMPONENT_REPS, stream, world, 10,
-                              TP_COMPONENT_REPS)
+            ar_us = _graph_us([lambda: ar.all_reduce(buf)], stream, world, TP_COMPONENT_LAUNCHES)
             import torch.distributed as dist
 
             nbuf = torch.zeros((B, cfg.hidden), dtype=torch.float16, device=device)
