@@ -302,6 +302,14 @@ def run_ours(args, rank, world, local):
         from torch_spyre_b200.tp import PeerAllReduce
 
         ar = PeerAllReduce(B * cfg.hidden, device=device)
+    nv = None
+    if world > 1:  # the NVLink SHARP all-reduce, where the GPUs offer multicast (decided collectively)
+        from torch_spyre_b200.tp import NvlsAllReduce
+
+        try:
+            nv = NvlsAllReduce(B * cfg.hidden, device=device)
+        except RuntimeError:
+            nv = None
 
     def step(s):
         if tp:
@@ -654,7 +662,7 @@ def _graph_us(fns, stream, world, launches):
     return max_over_ranks(us, world)
 
 
-def tp_parity_check(rank, world, device, ar, fused_ok):
+def tp_parity_check(rank, world, device, ar, fused_ok, nv=None):
     """Checker, run after the timed region: one small head-sharded step (ragged
     contexts, partial pages) through each path the block times, against the
     CPU oracle (the reference's CPU eager decode of all heads, then the full
@@ -678,6 +686,8 @@ def tp_parity_check(rank, world, device, ar, fused_ok):
         ys["peer"] = tp_decode_step(*step_args, allreduce=ar).clone()
         if fused_ok:
             ys["fused"] = tp_decode_step(*step_args, allreduce=ar, fused_oproj=True).clone()
+        if nv is not None:
+            ys["nvls"] = tp_decode_step(*step_args, allreduce=nv).clone()
         ys["nccl"] = tp_decode_step(*step_args)
     torch.cuda.synchronize(device)
     ref = tp_step_cpu(full.q, full.k_pool, full.v_pool, full.block_table, full.context_lens, w_o)
@@ -686,8 +696,9 @@ def tp_parity_check(rank, world, device, ar, fused_ok):
         y = y.cpu().float()
         ok &= bool(torch.allclose(y, ref, atol=TP_ATOL, rtol=TP_RTOL))
         err = max(err, float((y - ref).abs().max()))
-    if ar is not None:
-        ok &= int(ar.error_flag.item()) == 0
+    for x in (ar, nv):
+        if x is not None:
+            ok &= int(x.error_flag.item()) == 0
     flag = -max_over_ranks(-float(ok), world)  # min over ranks
     return flag == 1.0, max_over_ranks(err, world), sorted(ys)
 
@@ -724,22 +735,32 @@ def run_tp_block(args, rank, world, local, device):
     attn = tsb.decode_attention(sets[0].q, sets[0].k_pool, sets[0].v_pool, sets[0].block_table,
                                 sets[0].context_lens).reshape(B, K)
     ar = PeerAllReduce(B * cfg.hidden, device=device)
+    nv = None
+    if world > 1:  # the NVLink SHARP all-reduce, where the GPUs offer multicast (decided collectively)
+        from torch_spyre_b200.tp import NvlsAllReduce
+
+        try:
+            nv = NvlsAllReduce(B * cfg.hidden, device=device)
+        except RuntimeError:
+            nv = None
     # the fused kernel needs hidden / (64 N) whole tiles and 128 co-resident CTAs
     fused_ok = cfg.hidden % (64 * world) == 0 and B <= 128
     partial = torch.empty((B, cfg.hidden), dtype=torch.float16, device=device)
     stream = torch.cuda.Stream(device)
 
-    def step(s, fused=False):
+    def step(s, fused=False, reducer=None):
         if world == 1 and not fused:
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o, out=partial)
         return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
-                              out=partial if fused else None, allreduce=ar, fused_oproj=fused)
+                              out=partial if fused else None, allreduce=reducer or ar, fused_oproj=fused)
 
     with torch.cuda.stream(stream):
         for s in sets:
             step(s)
             if fused_ok:
                 step(s, fused=True)
+            if nv is not None:
+                step(s, reducer=nv)
         stream.synchronize()
     barrier(world)
     reps = max(1, -(-TP_STEPS // n_sets))
@@ -752,6 +773,8 @@ def run_tp_block(args, rank, world, local, device):
         step_us = _graph_us([lambda s=s: step(s) for s in sets], stream, world, n_steps)
         fused_us = (_graph_us([lambda s=s: step(s, True) for s in sets], stream, world, n_steps)
                     if fused_ok else None)
+        nvls_step_us = (_graph_us([lambda s=s: step(s, reducer=nv) for s in sets], stream, world, n_steps)
+                        if nv is not None else None)
         dec_us = _graph_us([lambda s=s: tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table,
                                                              s.context_lens) for s in sets],
                            stream, world, n_steps)
@@ -759,11 +782,15 @@ def run_tp_block(args, rank, world, local, device):
                              stream, world, TP_COMPONENT_LAUNCHES)
         fused_alone_us = (_graph_us([lambda w=w: ar.oproj_all_reduce(attn, w, out=partial) for w in w_rot],
                                     stream, world, TP_COMPONENT_LAUNCHES) if fused_ok else None)
-        ar_us = nccl_us = None
+        ar_us = nccl_us = nvls_us = None
         if world > 1:
             buf = ar.buffer((B, cfg.hidden))
             buf.zero_()
             ar_us = _graph_us([lambda: ar.all_reduce(buf)], stream, world, TP_COMPONENT_LAUNCHES)
+            if nv is not None:
+                nbuf_mc = nv.buffer((B, cfg.hidden))
+                nbuf_mc.zero_()
+                nvls_us = _graph_us([lambda: nv.all_reduce(nbuf_mc)], stream, world, TP_COMPONENT_LAUNCHES)
             import torch.distributed as dist
 
             nbuf = torch.zeros((B, cfg.hidden), dtype=torch.float16, device=device)
@@ -791,15 +818,20 @@ def run_tp_block(args, rank, world, local, device):
         "oproj_us": round(oproj_us, 2), "oproj": "cuBLAS (torch.matmul) into the peer buffer",
         "oproj_fused_allreduce_us": round(fused_alone_us, 2) if fused_alone_us else None,
         "allreduce_us": round(ar_us, 2) if ar_us else None,
+        "allreduce_nvls_us": round(nvls_us, 2) if nvls_us else None,
+        "value_nvls": round(B / (nvls_step_us / 1e6), 1) if nvls_step_us else None,
+        "ms_per_step_nvls": round(nvls_step_us / 1e3, 5) if nvls_step_us else None,
         "allreduce_nccl_us": round(nccl_us, 2) if nccl_us else None,
         "gpu_launches": res["steps"] * (2 if world > 1 else 1),
         "clocks": clk.summary(),
     })
-    ok, err, paths = tp_parity_check(rank, world, device, ar if world > 1 else None, fused_ok)
+    ok, err, paths = tp_parity_check(rank, world, device, ar if world > 1 else None, fused_ok, nv)
     res.update({"tp_parity_ok": ok, "tp_parity_max_abs_err": round(err, 6), "tp_parity_paths": paths,
                 "tp_parity_case": f"B={len(TP_PARITY_CTX)} ctx {TP_PARITY_CTX}, all heads, hidden {cfg.hidden}, "
                                   f"vs CPU oracle (decode x W_o in fp32), atol {TP_ATOL} rtol {TP_RTOL}"})
     del w_rot
+    if nv is not None:
+        nv.close()
     ar.close()
     return res
 

@@ -440,6 +440,31 @@ B200KV_API int b200kv_peer_allreduce_f16(void *const *peer_buffers, int32_t rank
                                          int64_t capacity_elems, int32_t ctas,
                                          int32_t *error_flag, void *stream);
 
+/* ------------------------------------------------------------------------ *
+ * Tensor-parallel all-reduce through NVLink SHARP (multimem).
+ *
+ * The same collective as b200kv_peer_allreduce_f16 -- the reference's TP
+ * SUM all-reduce of one tensor (SpyreCCLBackend::allreduce,
+ * torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494) -- with the adds done
+ * inside the NVSwitch: every element is reduced once by its owning rank
+ * (multimem.ld_reduce, fp32 accumulation, rounded once to fp16) and the sum
+ * is multicast to every rank (multimem.st), so all ranks end with the same
+ * bits.  The caller allocates, on every rank, the data buffer of num_elems
+ * fp16 at the same offset of memory bound to one NVLink multicast object
+ * (e.g. PyTorch symmetric memory) and passes its multicast address, plus a
+ * separate zero-initialised signal area of b200kv_nvls_signal_bytes() per
+ * rank, mapped into every rank (table of all ranks' areas, own included, in
+ * rank order, 256-byte aligned).  num_elems must be a multiple of 8 * world;
+ * ctas in [0, 64] (0 = 32).  The data buffer holds the partial on entry and
+ * the sum on exit.  Every rank must make the same calls in the same order;
+ * waits are bounded (2 s, then B200KV_DEVERR_TIMEOUT in error_flag and the
+ * output is undefined).  Calls replay correctly from CUDA graphs.
+ * ------------------------------------------------------------------------ */
+B200KV_API int64_t b200kv_nvls_signal_bytes(void);
+B200KV_API int b200kv_nvls_allreduce_f16(void *multicast_data, void *const *signal_areas,
+                                         int32_t rank, int32_t world, int64_t num_elems,
+                                         int32_t ctas, int32_t *error_flag, void *stream);
+
 /* Fused o_proj GEMM + SUM all-reduce of the tensor-parallel step, one kernel
  * per rank: out[b, n] = sum over ranks of sum_k attn[b, k] * w[n, k]
  * (attn fp16 [batch, k] row stride attn_stride_b; w fp16 [hidden, k] row

@@ -4,13 +4,14 @@
 Each rank runs the CUDA decode kernel on its KV-head shard and its o_proj
 partial, then the SUM all-reduce (the reference's TP collective,
 SpyreCCLBackend::allreduce, torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494)
-by each of the three paths: NCCL, the peer-memory all-reduce kernel, and the
-fused o_proj + all-reduce kernel.  Every result must match the oracle -- the
+by each path: NCCL, the peer-memory all-reduce kernel, the fused o_proj +
+all-reduce kernel, and (where the GPUs offer NVLink multicast) the NVLink
+SHARP all-reduce kernel.  Every result must match the oracle -- the
 reference's CPU eager decode of all heads followed by the full o_proj in fp32
 -- within 1e-2 abs + 1e-2 rel (the decode tolerance carried through an fp16
 attention output and fp16 partials summed over K = 8192 / N products), and
-every rank must hold the same bits.  Ranks are spawned processes with NVLS off
-(the kernels use plain peer stores).
+every rank must hold the same bits.  Ranks are spawned processes (NCCL's own
+NVLS off) that all run to their clean exit.
 """
 
 import os
@@ -49,7 +50,7 @@ def _worker(rank, world, port, results):
     import torch.distributed as dist
 
     import torch_spyre_b200  # noqa: F401
-    from torch_spyre_b200.tp import HeadShard, PeerAllReduce, tp_decode_step
+    from torch_spyre_b200.tp import HeadShard, NvlsAllReduce, PeerAllReduce, tp_decode_step
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -69,7 +70,17 @@ def _worker(rank, world, port, results):
         torch.cuda.synchronize()
         flag = int(ar.error_flag.item())
         ar.close()
-        results[rank] = ("ok", {"nccl": y_nccl, "peer": y_peer, "fused": y_fused}, flag)
+        ys = {"nccl": y_nccl, "peer": y_peer, "fused": y_fused}
+        try:  # the NVLink SHARP all-reduce, where the GPUs offer multicast
+            nv = NvlsAllReduce(128 * HIDDEN)
+        except RuntimeError:
+            nv = None
+        if nv is not None:
+            ys["nvls"] = tp_decode_step(*args, allreduce=nv).cpu().clone()
+            torch.cuda.synchronize()
+            flag |= int(nv.error_flag.item())
+            nv.close()
+        results[rank] = ("ok", ys, flag)
     except Exception as e:
         results[rank] = ("error", f"{type(e).__name__}: {e}")
     finally:
@@ -101,6 +112,6 @@ def test_tp_step_matches_oracle(world):
         assert flag == 0
         for path, y in ys.items():
             torch.testing.assert_close(y.float(), ref, atol=ATOL, rtol=RTOL, msg=lambda m: f"{path}: {m}")
-    for path in ("nccl", "peer", "fused"):
+    for path in res[0][1]:
         for r in range(1, world):
             assert torch.equal(res[0][1][path], res[r][1][path]), f"{path}: ranks 0 and {r} differ"

@@ -29,6 +29,7 @@ SOURCES = [
     "stick_relayout.cu",
     "fp8_ops.cu",
     "peer_allreduce.cu",
+    "nvls_allreduce.cu",
     "rope.cu",
     "lse_combine.cu",
     "oproj_allreduce.cu",

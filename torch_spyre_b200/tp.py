@@ -192,6 +192,100 @@ class PeerAllReduce:
         self._opened = []
 
 
+class NvlsAllReduce:
+    """SUM all-reduce of fp16 tensors of up to ``capacity`` elements through
+    NVLink SHARP (libb200kv ``b200kv_nvls_allreduce_f16``): the NVSwitch adds
+    the ranks' values and multicasts the sum.
+
+    The buffer is PyTorch symmetric memory (one allocation per rank, bound to
+    an NVLink multicast object by ``rendezvous``): the data region first, then
+    the kernel's signal area.  PyTorch only provides that memory and its
+    mapping; the collective is this library's kernel.  Usage matches
+    :class:`PeerAllReduce`: ``buffer(shape)`` is the view a producer writes,
+    ``all_reduce(view)`` sums it in place across ranks on the current stream;
+    every rank makes the same calls; graph replays are supported; waits are
+    bounded (B200KV_DEVERR_TIMEOUT in ``error_flag``).  Raises RuntimeError if
+    the GPUs offer no multicast (``available()`` tells beforehand).
+    """
+
+    def __init__(self, capacity: int, group=None, device: Optional[torch.device] = None, ctas: int = 32):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        q = 8 * self.world
+        self.capacity = -(-int(capacity) // q) * q
+        self.ctas = int(ctas)
+        lib = _lib.lib()
+        self._data_bytes = -(-self.capacity * 2 // 256) * 256
+        sig = int(lib.b200kv_nvls_signal_bytes())
+        with torch.cuda.device(self.device):
+            try:
+                self._buf = symm_mem.empty(self._data_bytes + sig, dtype=torch.uint8, device=self.device)
+                self._hdl = symm_mem.rendezvous(self._buf, self.group.group_name)
+                mc = int(self._hdl.multicast_ptr)
+            except Exception:  # no symmetric memory here: no multicast either
+                self._buf = self._hdl = None
+                mc = 0
+            # every rank sees the same answer; decide collectively so all raise or none
+            flag = torch.tensor([1 if mc else 0], dtype=torch.int32, device=self.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+            if not int(flag.item()):
+                self._hdl = None
+                self._buf = None
+                raise RuntimeError("NVLink multicast is not available on these GPUs")
+            self._buf[self._data_bytes:].zero_()
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._mc = mc
+        self._signals = (ctypes.c_void_p * self.world)(*[int(p) + self._data_bytes for p in self._hdl.buffer_ptrs])
+        self._data = self._buf[: self.capacity * 2].view(torch.float16)
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    @staticmethod
+    def available(group=None) -> bool:
+        """Whether NVLink multicast buffers can be made for ``group`` (collective)."""
+        import torch.distributed as dist
+
+        try:
+            NvlsAllReduce(8 * dist.get_world_size(group), group=group).close()
+            return True
+        except RuntimeError:
+            return False
+
+    def buffer(self, shape) -> torch.Tensor:
+        """A view of the data region (fp16, contiguous) of the given shape."""
+        n = 1
+        for d in shape:
+            n *= int(d)
+        if n > self.capacity:
+            raise ValueError(f"{n} elements exceed the multicast buffer capacity {self.capacity}")
+        return self._data[:n].view(*shape)
+
+    def all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        """Sums ``t`` (a view from ``buffer``) over the ranks, in place."""
+        if t.dtype != torch.float16 or not t.is_contiguous() or t.data_ptr() != self._data.data_ptr():
+            raise ValueError("all_reduce takes a contiguous fp16 view returned by buffer()")
+        _lib.call("b200kv_nvls_allreduce_f16", self._mc, self._signals, self.rank, self.world, t.numel(),
+                  self.ctas, self.error_flag.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        return t
+
+    def close(self) -> None:
+        """Releases the buffer after a barrier (no rank may still use it)."""
+        import torch.distributed as dist
+
+        if self._buf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._data = None
+        self._hdl = None
+        self._buf = None
+
+
 AttnFn = Callable[..., torch.Tensor]
 
 
