@@ -71,6 +71,13 @@ def parse_args():
                    help="tp70b at N > 1: capture the step, NCCL all-reduce included, in a CUDA graph")
     p.add_argument("--no-tp", action="store_true",
                    help="skip the head-sharded tp70b block that every decode workload's line carries")
+    p.add_argument("--no-early-start", action="store_true",
+                   help="launch every decode without B200KV_DECODE_INPUTS_READY")
+    p.add_argument("--kv-shards", type=int, default=1,
+                   help="tp70b on one GPU: run the share one rank of an N-way head split holds (8 / N KV heads)")
+    p.add_argument("--profile-launches", type=int, default=0,
+                   help="run K eager decode launches of input set 0 and print its algorithmic bytes (for a "
+                        "profiler capture of one launch; no timing)")
     return p.parse_args()
 
 
@@ -173,14 +180,20 @@ def hbm_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic_ratio(kernel: str, workload: str):
-    """DRAM bytes / algorithmic bytes of one launch, from the committed ncu
-    summary of this kernel and workload (None if there is none)."""
-    p = REPO / "profiles" / f"{kernel}_{workload}.md"
+def profiled_traffic(kernel: str, workload: str, bytes_per_launch: float):
+    """(DRAM bytes per launch, where they come from) for this kernel and
+    workload: ncu's dram__bytes_read.sum + dram__bytes_write.sum of one
+    captured launch, from the machine-readable summary
+    profiles/<kernel>_<workload>.json, scaled from that launch's algorithmic
+    bytes to this run's.  (None, None) if no capture exists."""
+    p = REPO / "profiles" / f"{kernel}_{workload}.json"
     if not p.exists():
-        return None
-    m = re.search(r"traffic_ratio\s*[=:]\s*([0-9.eE+]+)", p.read_text())
-    return float(m.group(1)) if m else None
+        return None, None
+    d = json.loads(p.read_text())
+    ratio = (d["dram__bytes_read.sum"] + d["dram__bytes_write.sum"]) / d["algorithmic_bytes"]
+    return round(ratio * bytes_per_launch), (
+        f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch = {ratio:.4f} x its algorithmic bytes "
+        f"(profiles/{p.name}), times this run's algorithmic bytes per launch")
 
 
 # ------------------------------------------------------------- CPU oracle ----
@@ -215,6 +228,14 @@ def rotating_sets(kv_bytes_of_set0: float) -> int:
     return min(n, 32)
 
 
+def set_tag(cfg, i: int, rank: int) -> str:
+    """Seed tag of input set i on a rank.  The head-sharded tp70b step has
+    the same sequences (context lengths, block tables) on every rank -- the
+    ranks hold different heads of them -- so its sets do not depend on the
+    rank; the replicated workloads give every rank its own batch."""
+    return f"set{i}" if cfg.name == "tp70b" else f"set{i}/rank{rank}"
+
+
 def workload_config(args, cfg, rank, world):
     """The `config` object of the JSON line, computed from the workload's
     seeded context lengths alone, so the repo arm and the reference arm print
@@ -222,27 +243,39 @@ def workload_config(args, cfg, rank, world):
     from torch_spyre_b200.workloads import context_lens_for
 
     tp = cfg.name == "tp70b"
-    hkv = cfg.num_kv_heads // world if tp else cfg.num_kv_heads
+    split = world * (args.kv_shards if tp else 1)
+    hkv = cfg.num_kv_heads // split if tp else cfg.num_kv_heads
     elt = 1 if args.kv_dtype == "fp8" else 2
 
     def kv_bytes(i):
-        return sum(context_lens_for(cfg, f"set{i}/rank{rank}")) * hkv * cfg.head_dim * 2 * elt
+        return sum(context_lens_for(cfg, set_tag(cfg, i, rank))) * hkv * cfg.head_dim * 2 * elt
 
     n_sets = rotating_sets(kv_bytes(0))
     kv = statistics.mean(kv_bytes(i) for i in range(n_sets))
-    B = len(context_lens_for(cfg, f"set0/rank{rank}"))
+    B = len(context_lens_for(cfg, set_tag(cfg, 0, rank)))
     ar = tp and world > 1 and args.allreduce in ("peer", "fused")
     graphed = not (tp and world > 1) or args.nccl_graph or ar
     return {"workload": args.workload, "description": cfg.description, "batch_per_rank": B,
             "global_batch": B if tp else B * world, "num_q_heads": cfg.num_q_heads,
             "num_kv_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim,
             "kv_heads_per_rank": hkv, "kv_dtype": args.kv_dtype,
-            "parallelism": (f"tp{world} (kv-head shards + "
-                            f"{'fused o_proj + peer-memory' if args.allreduce == 'fused' and ar else 'peer-memory' if ar else 'NCCL'}"
-                            " all-reduce)" if tp else f"dp{world} (sequence shards)"),
+            "parallelism": ((f"tp{world} (kv-head shards + "
+                             f"{'fused o_proj + peer-memory' if args.allreduce == 'fused' and ar else 'peer-memory' if ar else 'NCCL'}"
+                             " all-reduce)") if tp and split == world
+                            else f"one rank's share of tp{split} (no all-reduce)" if tp
+                            else f"dp{world} (sequence shards)"),
             "l2": f"{n_sets} rotating input sets, {kv / 1e6:.1f} MB KV read per step (L2 126 MB)",
             "graphs": (f"up to {max(1, 16 // n_sets) * n_sets} steps per graph replay" if graphed
-                       else "eager (NCCL step)")}
+                       else "eager (NCCL step)"),
+            "decode_launch": ("B200KV_DECODE_INPUTS_READY (inputs written before the previous step)"
+                              if not tp and args.kv_dtype == "fp16" and not args.no_early_start else "default")}
+
+
+def profile_key(args) -> str:
+    """Workload name of the profile summaries: tp70b shares carry their split."""
+    if args.workload == "tp70b" and args.kv_shards > 1:
+        return f"tp70b_kv{8 // args.kv_shards}"
+    return args.workload
 
 
 # ----------------------------------------------------------------- ours -----
@@ -253,9 +286,9 @@ def build_inputs(cfg, rank, world, n_sets, device, start=0, kv_dtype="fp16"):
     for i in range(start, start + n_sets):
         if cfg.name == "tp70b":
             hkv = cfg.num_kv_heads // world
-            inp = make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}", num_kv_heads=hkv, ctx=None)
+            inp = make_decode_inputs(cfg, device=device, seed_tag=set_tag(cfg, i, rank), num_kv_heads=hkv, ctx=None)
         else:
-            inp = make_decode_inputs(cfg, device=device, seed_tag=f"set{i}/rank{rank}")
+            inp = make_decode_inputs(cfg, device=device, seed_tag=set_tag(cfg, i, rank))
         if kv_dtype == "fp8":  # the same step over e4m3 pages (quantized on the device)
             inp = quantize_decode_inputs(inp)
             torch.cuda.synchronize(device)
@@ -272,14 +305,29 @@ def run_ours(args, rank, world, local):
     steps = args.steps or DEFAULT_STEPS[args.workload]
     warmup = max(3, args.warmup if args.warmup is not None else 20)
     tp = cfg.name == "tp70b"
-    if tp and cfg.num_kv_heads % world:
+    # tp70b: the KV heads split over `split` ranks (kv_shards > 1 runs one
+    # rank's share of a wider split on this rank's GPU)
+    split = world * (args.kv_shards if tp else 1)
+    if tp and cfg.num_kv_heads % split:
         raise SystemExit(f"tp70b needs N dividing {cfg.num_kv_heads}")
 
     # how many rotating input sets keep each step's reads out of L2
     fp8 = args.kv_dtype == "fp8"
-    probe = build_inputs(cfg, rank, world, 1, device, kv_dtype=args.kv_dtype)[0]
-    n_sets = rotating_sets(probe.kv_bytes)
-    sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1, kv_dtype=args.kv_dtype)
+    probe = build_inputs(cfg, rank, split, 1, device, kv_dtype=args.kv_dtype)[0]
+    if args.profile_launches > 0:
+        # a fixed launch for a profiler: K eager launches over input set 0
+        for _ in range(args.profile_launches):
+            tsb.decode_attention(probe.q, probe.k_pool, probe.v_pool, probe.block_table, probe.context_lens,
+                                 k_scale=probe.k_scale, v_scale=probe.v_scale)
+        torch.cuda.synchronize(device)
+        if rank == 0:
+            print(json.dumps({"profile_launches": args.profile_launches, "workload": profile_key(args),
+                              "kv_dtype": args.kv_dtype, "algorithmic_bytes_per_launch": int(probe.step_bytes),
+                              "kv_bytes_per_launch": int(probe.kv_bytes), "input_set": 0}), flush=True)
+        return
+    # every rank replays the same number of steps per graph (a TP step holds a collective)
+    n_sets = int(max_over_ranks(rotating_sets(probe.kv_bytes), world))
+    sets = [probe] + build_inputs(cfg, rank, split, n_sets - 1, device, start=1, kv_dtype=args.kv_dtype)
     step_bytes = statistics.mean(s.step_bytes for s in sets)
     kv_bytes = statistics.mean(s.kv_bytes for s in sets)
     B = len(sets[0].ctx)
@@ -288,7 +336,7 @@ def run_ours(args, rank, world, local):
     if tp:
         from torch_spyre_b200.tp import HeadShard, tp_decode_step
 
-        shard = HeadShard(rank, world, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
+        shard = HeadShard(rank, split, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
         hidden = cfg.hidden
         g = torch.Generator(device=device)
         g.manual_seed(1234 + rank)
@@ -316,12 +364,16 @@ def run_ours(args, rank, world, local):
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
                                   out=partial if ar is None or fused else None, k_scale=s.k_scale,
                                   v_scale=s.v_scale, allreduce=ar, fused_oproj=fused)
-        return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
-                                    v_scale=s.v_scale)
+        return decode_only(s)
+
+    # The steps' pools, block tables and context lengths are written once,
+    # before any step: each decode may plan and start its page loads while the
+    # previous step's kernel finishes (B200KV_DECODE_INPUTS_READY; fp16 pages).
+    ready = not fp8 and not tp and not args.no_early_start
 
     def decode_only(s):
         return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
-                                    v_scale=s.v_scale)
+                                    v_scale=s.v_scale, inputs_ready=ready)
 
     stream = torch.cuda.Stream(device)
 
@@ -383,13 +435,14 @@ def run_ours(args, rank, world, local):
 
     with torch.cuda.stream(stream):
         eager_step = None if graphed else step
-        run_steps(step_multi if graphed else None, step_single if graphed else None, warmup, eager_step)
         t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        stream.synchronize()
-        barrier(world)
-        torch.cuda.synchronize()
         with ClockSampler(local if world > 1 else 0) as clk:
             time.sleep(0.25)  # let the sampler start
+            # the warm-up steps run right before the timed ones (no idle gap between them)
+            run_steps(step_multi if graphed else None, step_single if graphed else None, warmup, eager_step)
+            stream.synchronize()
+            barrier(world)
+            torch.cuda.synchronize()
             t_all0.record(stream)
             spans = run_steps(step_multi if graphed else None, step_single if graphed else None, steps,
                               eager_step, events=True)
@@ -420,12 +473,10 @@ def run_ours(args, rank, world, local):
     # achieved bandwidth of the decode kernel (the only launch of a replicated
     # step; timed on its own for tp70b)
     achieved = step_bytes / (launch_ms / 1e3) / 1e9
+    traffic, traffic_src = profiled_traffic(kernel, profile_key(args), step_bytes)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                "traffic": (round(ratio * step_bytes) if (ratio := profiled_traffic_ratio(kernel, args.workload))
-                            else None),
-                "traffic_source": (f"ncu dram__bytes_read+write / algorithmic = {ratio} (profiles/{kernel}_"
-                                   f"{args.workload}.md), times this run's bytes per launch") if ratio else None,
+                "traffic": traffic, "traffic_source": traffic_src,
                 "kernel": kernel, "algorithmic_bytes_per_launch": int(step_bytes),
                 "mean_launch_ms": round(launch_ms, 5)}
 
@@ -720,7 +771,7 @@ def run_tp_block(args, rank, world, local, device):
     if cfg.num_kv_heads % world:
         return {"error": f"{world} ranks do not divide {cfg.num_kv_heads} KV heads"}
     probe = build_inputs(cfg, rank, world, 1, device)[0]
-    n_sets = min(32, max(1, math.ceil(3 * L2_BYTES / probe.kv_bytes)))
+    n_sets = int(max_over_ranks(rotating_sets(probe.kv_bytes), world))  # same on every rank
     sets = [probe] + build_inputs(cfg, rank, world, n_sets - 1, device, start=1)
     B = len(sets[0].ctx)
     shard = HeadShard(rank, world, cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim)
@@ -808,6 +859,8 @@ def run_tp_block(args, rank, world, local, device):
             nccl_us = max_over_ranks(1e3 * a.elapsed_time(b) / 200, world)
     peak, peak_kind = hbm_peak()
     dec_bytes = statistics.mean(s.step_bytes for s in sets)
+    dec_traffic, dec_traffic_src = profiled_traffic("decode_kernel", f"tp70b_kv{cfg.num_kv_heads // world}"
+                                                    if world > 1 else "tp70b", dec_bytes)
     res.update({
         "value": round(B / (step_us / 1e6), 1), "unit": "tokens/s", "ms_per_step": round(step_us / 1e3, 5),
         "value_fused": round(B / (fused_us / 1e6), 1) if fused_us else None,
@@ -815,6 +868,7 @@ def run_tp_block(args, rank, world, local, device):
         "decode_us": round(dec_us, 2),
         "decode_frac": round(dec_bytes / (dec_us / 1e6) / 1e9 / peak, 4), "decode_peak_gbs": peak,
         "decode_peak_source": peak_kind, "decode_bytes_per_launch": int(dec_bytes),
+        "decode_traffic": dec_traffic, "decode_traffic_source": dec_traffic_src,
         "oproj_us": round(oproj_us, 2), "oproj": "cuBLAS (torch.matmul) into the peer buffer",
         "oproj_fused_allreduce_us": round(fused_alone_us, 2) if fused_alone_us else None,
         "allreduce_us": round(ar_us, 2) if ar_us else None,
@@ -896,6 +950,7 @@ def run_relayout(args, rank, world, local):
     launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
     peak, kind = hbm_peak()
     achieved = step_bytes / (launch_ms / 1e3) / 1e9
+    rl_traffic, rl_src = profiled_traffic("relayout_kernels", "relayout", step_bytes)
     line = {
         "metric": "KV relayout/append bytes moved per second", "value": round(step_bytes * world * steps / total_ms / 1e6, 1),
         "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": warmup,
@@ -905,10 +960,7 @@ def run_relayout(args, rank, world, local):
                    "append_tokens": n, "l2": f"{2 * bulk / 1e6:.0f} MB per direction > 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": kind,
-                     "traffic": (round(ratio * step_bytes) if (ratio := profiled_traffic_ratio(
-                         "relayout_kernels", "relayout")) else None),
-                     "traffic_source": "ncu dram__bytes_read+write / algorithmic of one step "
-                                       "(profiles/relayout_kernels_relayout.md), times this run's bytes",
+                     "traffic": rl_traffic, "traffic_source": rl_src,
                      "kernel": "kv_append + relayout_kernel<0> + relayout_kernel<1> (one step)",
                      "algorithmic_bytes_per_launch": step_bytes, "mean_launch_ms": round(launch_ms, 5)},
         "gpu_launches": 3 * steps,

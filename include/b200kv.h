@@ -215,6 +215,31 @@ B200KV_API int b200kv_decode_attention_append_f16(
     void *workspace, int64_t workspace_bytes, int32_t *error_flag,
     void *stream);
 
+/* Decode attention with options: the arguments of b200kv_decode_attention_f16
+ * plus `flags`, the same computation and result.
+ *   B200KV_DECODE_INPUTS_READY  the pools, block table and context lengths were
+ *     written before the preceding kernel on `stream` began (q may still be
+ *     written by it).  The decode kernel is launched as a programmatic
+ *     dependent of that kernel; with this flag each CTA plans its work and
+ *     starts loading its first pages while the preceding kernel finishes, and
+ *     only q, the scales, the workspace and the outputs wait for it.  Without
+ *     the flag (or under the CUDA-core kernel) everything waits.  A kernel of
+ *     this library that writes pool rows (the fused append) lets its
+ *     successors start only after it completes.
+ * Same reference interface as b200kv_decode_attention_f16
+ * (decompositions.py:523-611); the flag has no reference counterpart (the
+ * reference has no programmatic dependent launch). */
+#define B200KV_DECODE_INPUTS_READY 1u
+B200KV_API int b200kv_decode_attention_ex_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
+    const void *v_pool, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    uint32_t flags, void *stream);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference:
  * it exists for callers that cannot call cudaMalloc or any allocator when they
  * launch decode (an engine replaying pre-planned memory, a plugin host that

@@ -181,3 +181,42 @@ def test_simt_kernel_variant_parity():
     env = dict(os.environ, B200KV_DECODE_KERNEL="simt", PYTHONPATH=repo)
     r = subprocess.run([sys.executable, "-c", code], env=env, cwd=repo, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "simt ok" in r.stdout, r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("name,hkv", [("gqa_b16", None), ("tp70b", 1), ("mha_b1", None)])
+def test_early_start_gives_the_same_bits(name, hkv):
+    """B200KV_DECODE_INPUTS_READY: plan and first page loads before the wait
+    for the preceding kernel.  Chained decodes where each one's q is the
+    previous one's output (written by a grid that lets its dependents start
+    early, so q must be read only after the wait), eager and graph-replayed,
+    give the same bits as the default launch."""
+    cfg = DECODE_CONFIGS[name]
+    kw = {"num_kv_heads": hkv} if hkv else {}
+    sets = [make_decode_inputs(cfg, device="cuda", seed_tag=f"early{i}", **kw) for i in range(2)]
+
+    def chain(ready):
+        outs, q = [], sets[0].q
+        for i in range(6):
+            s = sets[i % 2]
+            q = tsb.decode_attention(q, s.k_pool, s.v_pool, s.block_table, s.context_lens, inputs_ready=ready)
+            outs.append(q)
+        return outs
+
+    ref = chain(False)
+    got = chain(True)
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        chain(True)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            graphed = chain(True)
+        g.replay()
+    stream.synchronize()
+    for a, b in zip(ref, graphed):
+        assert torch.equal(a, b)
+    first = opa.decode_attention_cpu(sets[0].q, sets[0].k_pool, sets[0].v_pool, sets[0].block_table,
+                                     sets[0].context_lens)
+    torch.testing.assert_close(got[0].cpu().float(), first.float(), atol=2e-3, rtol=1e-2)

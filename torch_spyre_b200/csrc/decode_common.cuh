@@ -50,6 +50,11 @@ struct DecodeArgs {
   // with rope_freqs[context_len - 1] ([max_pos][2][2][64] fp16, rope.cuh).
   const __half *rope_freqs = nullptr;
   int64_t rope_max_pos = 0;
+  // Early start (not with the fused append): the pools, block table and
+  // context lengths were written before the preceding kernel on the stream
+  // began, so the plan and the first stages' page loads may run before
+  // griddepcontrol.wait; q, the scales, the workspace and the outputs wait.
+  int early = 0;
 };
 
 struct WorkspaceLayout {
@@ -423,9 +428,10 @@ __device__ __forceinline__ void combine_online_warp_from(const DecodeArgs &a, in
           const float mn = fmaxf(M[g], m);
           const float w_old = M[g] == -CUDART_INF_F ? 0.f : exp2f(M[g] - mn);
           const float w_new = exp2f(m - mn);
-          Ls[g] = Ls[g] * w_old + ml[j][g].y * w_new;
+          // explicit roundings: every merge path computes the same bits
+          Ls[g] = fmaf(Ls[g], w_old, __fmul_rn(ml[j][g].y, w_new));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) acc[g][k] = acc[g][k] * w_old + ov[j][g][k] * w_new;
+          for (int k = 0; k < 4; ++k) acc[g][k] = fmaf(acc[g][k], w_old, __fmul_rn(ov[j][g][k], w_new));
           M[g] = mn;
         }
       }

@@ -78,7 +78,7 @@ constexpr int kQSlotBytes = 8 * kQRowBytes;
 // every warp's unnormalised O^T [128 d][8 h], its (max, sum) per head and the
 // piece's identity.  Two buffers let the consumers run a piece ahead.
 struct PieceHeader {
-  int b, kvh, pair, nsplit, slot, end, tail;
+  int b, kvh, pair, nsplit, slot, end, tail, own_first;
 };
 constexpr int kPieceO = 0;                                   // float [4][128][8]
 constexpr int kPieceML = kConsumerWarps * kHeadDim * 8 * 4;  // float2 [4][8]
@@ -111,6 +111,7 @@ constexpr int kDescPage = 4;   // the stage holds a page (an empty sequence has 
 constexpr int kDescEnd = 8;    // no more work for this CTA
 constexpr int kDescNew = 16;   // the stage carries the appended token's K/V rows
 constexpr int kDescTail = 32;  // the page belongs to the CTA's final piece
+constexpr int kDescOwnFirst = 64;  // the piece holds its pair's lowest partial slot
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -197,12 +198,18 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
     fence_mbar_init();
   }
-  // Programmatic dependent launch: nothing above reads global memory; wait for
-  // the preceding grid on the stream to finish (a no-op when this launch has
-  // no programmatic predecessor), then let the next grid be scheduled so its
-  // CTAs take over SMs as soon as ours exit.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Programmatic dependent launch.  Nothing above reads global memory.  By
+  // default every thread waits here for the preceding grid on the stream to
+  // finish (a no-op when this launch has no programmatic predecessor).  With
+  // an early start the plan and the producer's first NST stages of page
+  // loads run before the wait -- they read only inputs written before the
+  // preceding kernel began -- and every role waits before it touches q, the
+  // scales, the workspace or the outputs.  The next grid may be scheduled at
+  // once so its CTAs take over SMs as soon as ours exit; the fused-append
+  // variant writes pool rows, so its dependents wait for its completion.
+  const bool early = !kAppend && a.early != 0;
+  if (!early) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!kAppend) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   build_unit_plan<kMmaThreads>(a, pl);  // synchronises the CTA
   const Partition P = make_partition(pl.total_items, static_cast<int>(gridDim.x));
   const int c = blockIdx.x;
@@ -216,11 +223,30 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const uint64_t policy = l2_policy_evict_first();
     int stage = 0;
     uint32_t phase = 0;
+    // early start: stages issued before griddepcontrol.wait get their q rows
+    // after it (their full barriers already expect those bytes)
+    bool waited = !early;
+    int issued = 0, ndefer = 0;
+    const __half *defer_q[NST];
+    int defer_stage[NST];
+    auto q_rows = [&](int st, const __half *qg) {
+      uint8_t *qs = smem + L::kQ + st * kQSlotBytes;
+#pragma unroll
+      for (int g = 0; g < G; ++g) bulk_load(qs + g * kQRowBytes, qg + g * a.q_sh, kHeadDim * 2, &full[st]);
+    };
+    auto finish_wait = [&]() {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      waited = true;
+      for (int j = 0; j < ndefer; ++j) q_rows(defer_stage[j], defer_q[j]);
+      ndefer = 0;
+    };
     auto emit_range = [&](int u_lo, int u_hi, int owner) {
       for (int u = u_lo; u < u_hi;) {
         const Piece pc = locate_piece(a, pl, P, u, u_hi, owner);
         u = pc.u_next;
-        const int tail_flag = u >= u_hi ? kDescTail : 0;
+        // kDescTail: the CTA's final piece; kDescOwnFirst: the piece starts at
+        // the pair's first page, so it holds the pair's lowest partial slot
+        const int tail_flag = (u >= u_hi ? kDescTail : 0) | (pc.p == 0 ? kDescOwnFirst : 0);
         const int npages = pc.p_end - pc.p;
         const int nstages = max(npages, 1);  // an empty sequence still takes one stage
         for (int base = 0; base < nstages; base += 32) {
@@ -259,17 +285,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               }
               if (has) {
                 if (i == 0) {  // the piece's q rows ride on its first page's barrier
-                  uint8_t *qs = smem + L::kQ + stage * kQSlotBytes;
                   const __half *qg = a.q + pc.b * a.q_sb + (pc.kvh * G) * a.q_sh;
-#pragma unroll
-                  for (int g = 0; g < G; ++g)
-                    bulk_load(qs + g * kQRowBytes, qg + g * a.q_sh, kHeadDim * 2, &full[stage]);
+                  if (waited) {
+                    q_rows(stage, qg);
+                  } else {
+                    defer_q[ndefer] = qg;
+                    defer_stage[ndefer] = stage;
+                    ++ndefer;
+                  }
                 }
                 uint8_t *dst = smem + stage * L::kStageBytes;
                 const int page = blk * a.hkv + pc.kvh;
                 tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
                 tma_load_3d(dst + L::kPage, &vmap, &full[stage], 0, 0, page, policy);
               }
+              if (!waited && ++issued == NST) finish_wait();
             }
             if (++stage == NST) {
               stage = 0;
@@ -280,6 +310,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       }
     };
     emit_range(P.lo(c), P.hi(c), c);
+    if (lane == 0 && !waited) finish_wait();
     if (lane == 0) {  // end marker
       mbar_wait_bounded(&empty[stage], phase ^ 1u, a.error_flag);
       descs[stage].flags = kDescEnd;
@@ -294,6 +325,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   // pair's completion ticket and, holding the last one, merges the pair's
   // partials.  Runs beside the consumers, which never wait for it unless it
   // falls two pieces behind.
+  if (early) asm volatile("griddepcontrol.wait;" ::: "memory");  // consumers and epilogue
   if (warp == kEpilogueWarp) {
     const float vsc = kFp8 ? __half2float(*a.v_scale) : 1.f;  // V dequantisation scale
     for (int k = 0;; ++k) {
@@ -347,7 +379,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       // counter; any lane that saw less sends the piece down the ticket path.
       // (tried on the CTA's final piece only: the pair it starts was finished
       // early by the next CTA, so it is almost always the pair's last)
-      if (hd.tail && __all_sync(0xffffffffu, ld_acquire_gpu(a.counters + hd.pair) == hd.nsplit - 1)) {
+      // Every merge folds the pair's partials in ascending slot order from the
+      // empty state, so the output bits do not depend on which piece merges:
+      // this shortcut starts from the piece's own state only when it holds
+      // the pair's lowest slot.
+      if (hd.tail && hd.own_first &&
+          __all_sync(0xffffffffu, ld_acquire_gpu(a.counters + hd.pair) == hd.nsplit - 1)) {
         int pj, w;
         pair_units(a, pl, hd.pair, &pj, &w);
         combine_online_warp_from<G>(a, hd.b, hd.kvh, pair_slots(P, hd.pair, pj, w), lane, hd.slot, mx, ls, acc);
@@ -447,6 +484,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       hd->slot = d.slot;
       hd->end = end;
       hd->tail = (d.flags & kDescTail) != 0;
+      hd->own_first = (d.flags & kDescOwnFirst) != 0;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&pfull[pb]);

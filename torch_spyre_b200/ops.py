@@ -39,6 +39,7 @@ from . import _lib
 from .layout import PAGE_TOKENS
 
 HEAD_DIM = 128
+DECODE_INPUTS_READY = 1  # B200KV_DECODE_INPUTS_READY
 
 # ---------------------------------------------------------------- helpers ---
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
@@ -114,6 +115,7 @@ def _decode_attention_op(
     scale: float,
     num_splits: int,
     error_flag: Optional[torch.Tensor],
+    inputs_ready: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     _require_cuda(q, k_pool, v_pool, block_table, context_lens)
     if q.dim() != 3 or q.dtype != torch.float16:
@@ -143,8 +145,7 @@ def _decode_attention_op(
     # An unsupported shape has no workspace size; the call below then reports
     # the precise reason from the library's own argument checks.
     ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
-    _lib.call(
-        "b200kv_decode_attention_f16",
+    args = (
         q.data_ptr(), q.stride(0), q.stride(1),
         k_pool.data_ptr(), v_pool.data_ptr(),
         block_table.data_ptr(), block_table.stride(0),
@@ -154,14 +155,18 @@ def _decode_attention_op(
         B, Hq, Hkv, D, NB, block_table.shape[1],
         float(scale), int(num_splits),
         ws.data_ptr(), ws.numel(),
-        _ptr(error_flag), _stream_ptr(q.device),
+        _ptr(error_flag),
     )
+    if inputs_ready:
+        _lib.call("b200kv_decode_attention_ex_f16", *args, DECODE_INPUTS_READY, _stream_ptr(q.device))
+    else:
+        _lib.call("b200kv_decode_attention_f16", *args, _stream_ptr(q.device))
     _maybe_check_flag(error_flag, "decode_attention")
     return out, lse
 
 
 @_decode_attention_op.register_fake
-def _(q, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag):
+def _(q, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag, inputs_ready=False):
     B, Hq, D = q.shape
     return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)
 
@@ -178,6 +183,7 @@ def decode_attention(
     error_flag: Optional[torch.Tensor] = None,
     k_scale: Optional[torch.Tensor] = None,
     v_scale: Optional[torch.Tensor] = None,
+    inputs_ready: bool = False,
 ):
     """Decode attention of one new token per sequence over the paged KV pools.
 
@@ -186,6 +192,11 @@ def decode_attention(
     ``k_scale`` / ``v_scale`` (one-element device tensors); block_table int32
     [B, max_blocks]; context_lens int32 [B].  Returns out [B, Hq, D] fp16 (and
     the natural-log LSE [B, Hq] fp32 when ``return_lse``).
+
+    ``inputs_ready`` (fp16 pools): the pools, block table and context lengths
+    were written before the preceding kernel on the stream began (q may be
+    written by it), so the kernel may plan and start its page loads while that
+    kernel finishes (B200KV_DECODE_INPUTS_READY).  Same result either way.
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
@@ -197,7 +208,8 @@ def decode_attention(
         )
     else:
         out, lse = torch.ops.b200kv.decode_attention(
-            q, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag
+            q, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag,
+            bool(inputs_ready)
         )
     return (out, lse) if return_lse else out
 
