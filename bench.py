@@ -268,7 +268,7 @@ def workload_config(args, cfg, rank, world):
             "graphs": (f"up to {max(1, 16 // n_sets) * n_sets} steps per graph replay" if graphed
                        else "eager (NCCL step)"),
             "decode_launch": ("B200KV_DECODE_INPUTS_READY (inputs written before the previous step)"
-                              if not tp and args.kv_dtype == "fp16" and not args.no_early_start else "default")}
+                              if args.kv_dtype == "fp16" and not args.no_early_start else "default")}
 
 
 def profile_key(args) -> str:
@@ -363,7 +363,8 @@ def run_ours(args, rank, world, local):
         if tp:
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
                                   out=partial if ar is None or fused else None, k_scale=s.k_scale,
-                                  v_scale=s.v_scale, allreduce=ar, fused_oproj=fused)
+                                  v_scale=s.v_scale, allreduce=ar, fused_oproj=fused,
+                                  inputs_ready=not fp8 and not args.no_early_start)
         return decode_only(s)
 
     # The steps' pools, block tables and context lengths are written once,
@@ -482,7 +483,10 @@ def run_ours(args, rank, world, local):
 
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar, fused)
+        # consecutive steps use different input sets (their own pools), so each
+        # fused append + decode may start its page loads under the previous one
+        e2e = run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar, fused,
+                      early=len(sets) >= 2 and not fp8 and not args.no_early_start)
 
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline_seconds > 0:
@@ -527,7 +531,7 @@ def run_ours(args, rank, world, local):
         ar.close()
 
 
-def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fused=False):
+def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fused=False, early=False):
     """Public-API decode step with host buffers: H2D inputs, append, decode, D2H.
 
     Each step's inputs (q, the new token's K/V rows, its slots, the block table
@@ -590,7 +594,7 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         else:  # one launch: append the new token's K/V rows and decode
             o = tsb.decode_attention_append(v["q"], v["k_new"], v["v_new"], s.k_pool, s.v_pool,
                                             v["block_table"], v["context_lens"], k_scale=s.k_scale,
-                                            v_scale=s.v_scale)
+                                            v_scale=s.v_scale, inputs_ready=early)
         return o
 
     def eager_round():  # each step in turn on one stream: upload, compute, download
@@ -675,7 +679,8 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
                      + ("captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
                         "overlapping the neighbouring steps' compute" if graph_ms is not None
                         else "eager")),
-            "eager": {"value": round(tokens / (eager_ms / 1e3), 1), "ms_per_step": round(eager_ms, 5)}}
+            "eager": {"value": round(tokens / (eager_ms / 1e3), 1), "ms_per_step": round(eager_ms, 5)},
+            "decode_launch": "B200KV_DECODE_INPUTS_READY" if early and not tp else "default"}
 
 
 # ------------------------------------------------ tensor-parallel block ----
@@ -799,11 +804,16 @@ def run_tp_block(args, rank, world, local, device):
     partial = torch.empty((B, cfg.hidden), dtype=torch.float16, device=device)
     stream = torch.cuda.Stream(device)
 
+    # the pools, block tables and context lengths are written once, before the
+    # steps: each step's decode may start its page loads while the previous
+    # step's all-reduce finishes (B200KV_DECODE_INPUTS_READY)
     def step(s, fused=False, reducer=None):
         if world == 1 and not fused:
-            return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o, out=partial)
+            return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o, out=partial,
+                                  inputs_ready=True)
         return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
-                              out=partial if fused else None, allreduce=reducer or ar, fused_oproj=fused)
+                              out=partial if fused else None, allreduce=reducer or ar, fused_oproj=fused,
+                              inputs_ready=True)
 
     with torch.cuda.stream(stream):
         for s in sets:

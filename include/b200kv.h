@@ -223,9 +223,9 @@ B200KV_API int b200kv_decode_attention_append_f16(
  *     dependent of that kernel; with this flag each CTA plans its work and
  *     starts loading its first pages while the preceding kernel finishes, and
  *     only q, the scales, the workspace and the outputs wait for it.  Without
- *     the flag (or under the CUDA-core kernel) everything waits.  A kernel of
- *     this library that writes pool rows (the fused append) lets its
- *     successors start only after it completes.
+ *     the flag (or under the CUDA-core kernel) everything waits.  Mind that
+ *     the fused append of this library writes pool rows: a decode of the same
+ *     pools right after it must not pass this flag.
  * Same reference interface as b200kv_decode_attention_f16
  * (decompositions.py:523-611); the flag has no reference counterpart (the
  * reference has no programmatic dependent launch). */
@@ -233,6 +233,25 @@ B200KV_API int b200kv_decode_attention_append_f16(
 B200KV_API int b200kv_decode_attention_ex_f16(
     const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
     const void *v_pool, const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    uint32_t flags, void *stream);
+
+/* Fused append + decode with options: the arguments of
+ * b200kv_decode_attention_append_f16 plus `flags`.  With
+ * B200KV_DECODE_INPUTS_READY the caller vouches that the pools (other than the
+ * rows this call appends), block table and context lengths were written before
+ * the preceding kernel on `stream` began; q and the new K/V rows may be written
+ * by it.  The kernel then plans and loads its first pages while that kernel
+ * finishes; the new rows, q and every write wait for it.  Same reference
+ * interface as b200kv_decode_attention_append_f16. */
+B200KV_API int b200kv_decode_attention_append_ex_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new,
+    const void *v_new, int64_t new_stride_b, int64_t new_stride_h, void *k_pool,
+    void *v_pool, const int32_t *block_table, int64_t block_table_stride,
     const int32_t *context_lens, void *out, int64_t out_stride_b,
     int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
     int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,

@@ -77,3 +77,32 @@ def test_fused_bad_block_skips_write_and_flags():
     blk1 = int(inp.block_table[1, 0])
     changed = (inp.k_pool != before).any(dim=(1, 2, 3, 4)).nonzero().flatten().tolist()
     assert changed == [blk1]  # only sequence 1's append landed
+
+
+def test_fused_early_start_same_bits():
+    """B200KV_DECODE_INPUTS_READY on the fused append: alternating two pool
+    sets (so no call's pools are written by the call right before it), the
+    outputs and the pools equal the default launches bit for bit."""
+    cfg = DECODE_CONFIGS["gqa_b16"]
+    ctx = [1, 63, 64, 65, 700, 4097]
+
+    def run(ready):
+        sets = [make_decode_inputs(cfg, device="cuda", ctx=ctx, seed_tag=f"early-append{i}") for i in range(2)]
+        g = torch.Generator(device="cuda").manual_seed(5)
+        outs = []
+        for step in range(6):
+            s = sets[step % 2]
+            k_new = torch.randn((len(ctx), 8, 128), generator=g, device="cuda", dtype=torch.float16)
+            v_new = torch.randn((len(ctx), 8, 128), generator=g, device="cuda", dtype=torch.float16)
+            outs.append(tsb.decode_attention_append(s.q, k_new, v_new, s.k_pool, s.v_pool, s.block_table,
+                                                    s.context_lens, inputs_ready=ready))
+        torch.cuda.synchronize()
+        return outs, sets
+
+    ref, ref_sets = run(False)
+    got, got_sets = run(True)
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    for a, b in zip(ref_sets, got_sets):
+        assert torch.equal(a.k_pool.view(torch.int16), b.k_pool.view(torch.int16))
+        assert torch.equal(a.v_pool.view(torch.int16), b.v_pool.view(torch.int16))

@@ -111,6 +111,23 @@ SIGNATURES = {
             _p, _p,  # error_flag, stream
         ],
     ),
+    "b200kv_decode_attention_append_ex_f16": (
+        ctypes.c_int,
+        [
+            _p, _i64, _i64,  # q, q_stride_b, q_stride_h
+            _p, _p, _i64, _i64,  # k_new, v_new, new_stride_b, new_stride_h
+            _p, _p,  # k_pool, v_pool
+            _p, _i64,  # block_table, block_table_stride
+            _p,  # context_lens
+            _p, _i64, _i64,  # out, out_stride_b, out_stride_h
+            _p,  # lse
+            _i64, _i64, _i64, _i64,  # batch, Hq, Hkv, head_dim
+            _i64, _i64,  # num_blocks, max_blocks_per_seq
+            _f32, _i64,  # scale, num_splits
+            _p, _i64,  # workspace, workspace_bytes
+            _p, ctypes.c_uint32, _p,  # error_flag, flags, stream
+        ],
+    ),
     "b200kv_decode_attention_f16_noalloc": (
         ctypes.c_int,
         [

@@ -148,7 +148,7 @@ static int decode_entry(
   a.part_ml = reinterpret_cast<float2 *>(ws + wl.ml_off);
   a.part_o = reinterpret_cast<float *>(ws + wl.o_off);
   a.error_flag = error_flag;
-  a.early = (flags & B200KV_DECODE_INPUTS_READY) != 0 && !append;
+  a.early = (flags & B200KV_DECODE_INPUTS_READY) != 0;
   if (append) {
     a.k_new = static_cast<const __half *>(k_new);
     a.v_new = static_cast<const __half *>(v_new);
@@ -222,6 +222,23 @@ extern "C" int b200kv_decode_attention_append_f16(
                       num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
                       workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
                       new_stride_h, true);
+}
+
+extern "C" int b200kv_decode_attention_append_ex_f16(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new, const void *v_new,
+    int64_t new_stride_b, int64_t new_stride_h, void *k_pool, void *v_pool,
+    const int32_t *block_table, int64_t block_table_stride, const int32_t *context_lens, void *out,
+    int64_t out_stride_b, int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq,
+    float scale, int64_t num_splits, void *workspace, int64_t workspace_bytes,
+    int32_t *error_flag, uint32_t flags, void *stream) {
+  if (flags & ~uint32_t(B200KV_DECODE_INPUTS_READY))
+    return set_error(B200KV_ERR_INVALID_ARG, "unknown flags 0x%x", flags);
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, k_new, v_new, new_stride_b,
+                      new_stride_h, true, false, nullptr, nullptr, nullptr, 0, flags);
 }
 
 extern "C" int b200kv_decode_attention_fp8(

@@ -50,10 +50,10 @@ struct DecodeArgs {
   // with rope_freqs[context_len - 1] ([max_pos][2][2][64] fp16, rope.cuh).
   const __half *rope_freqs = nullptr;
   int64_t rope_max_pos = 0;
-  // Early start (not with the fused append): the pools, block table and
-  // context lengths were written before the preceding kernel on the stream
-  // began, so the plan and the first stages' page loads may run before
-  // griddepcontrol.wait; q, the scales, the workspace and the outputs wait.
+  // Early start: the pools, block table and context lengths were written
+  // before the preceding kernel on the stream began, so the plan and the
+  // first stages' page loads may run before griddepcontrol.wait; q, the
+  // appended rows, the scales, the workspace and every write wait.
   int early = 0;
 };
 
@@ -363,6 +363,11 @@ __device__ __forceinline__ void store_out(const DecodeArgs &a, int b, int h, int
                                           float l) {
   a.out[b * a.o_sb + h * a.o_sh + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
 }
+// The same with the reciprocal of the sum (one division per head).
+__device__ __forceinline__ float inv_sum(float l) { return l > 0.f ? __frcp_rn(l) : 0.f; }
+__device__ __forceinline__ void store_out_inv(const DecodeArgs &a, int b, int h, int d, float acc, float inv) {
+  a.out[b * a.o_sb + h * a.o_sh + d] = __float2half_rn(__fmul_rn(acc, inv));
+}
 __device__ __forceinline__ void store_lse(const DecodeArgs &a, int b, int h, float m, float l) {
   if (a.lse)
     a.lse[static_cast<int64_t>(b) * a.hq + h] = l > 0.f ? (m + log2f(l)) * kLn2 : -CUDART_INF_F;
@@ -439,8 +444,9 @@ __device__ __forceinline__ void combine_online_warp_from(const DecodeArgs &a, in
   const int h0 = kvh * G;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
+    const float inv = inv_sum(Ls[g]);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) store_out(a, b, h0 + g, lane + 32 * k, acc[g][k], Ls[g]);
+    for (int k = 0; k < 4; ++k) store_out_inv(a, b, h0 + g, lane + 32 * k, acc[g][k], inv);
     if (lane == 0) store_lse(a, b, h0 + g, M[g], Ls[g]);
   }
 }

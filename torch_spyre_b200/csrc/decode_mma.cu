@@ -204,12 +204,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   // an early start the plan and the producer's first NST stages of page
   // loads run before the wait -- they read only inputs written before the
   // preceding kernel began -- and every role waits before it touches q, the
-  // scales, the workspace or the outputs.  The next grid may be scheduled at
-  // once so its CTAs take over SMs as soon as ours exit; the fused-append
-  // variant writes pool rows, so its dependents wait for its completion.
-  const bool early = !kAppend && a.early != 0;
+  // appended rows, the scales, the workspace, the pools' new rows or the
+  // outputs.  The next grid may be scheduled at once so its CTAs take over
+  // SMs as soon as ours exit (it waits for this grid before it reads what
+  // this grid writes, unless its own caller vouched that it does not).
+  const bool early = a.early != 0;
   if (!early) asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (!kAppend) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   build_unit_plan<kMmaThreads>(a, pl);  // synchronises the CTA
   const Partition P = make_partition(pl.total_items, static_cast<int>(gridDim.x));
   const int c = blockIdx.x;
@@ -228,16 +229,25 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     bool waited = !early;
     int issued = 0, ndefer = 0;
     const __half *defer_q[NST];
+    int64_t defer_new[NST];  // offset of the appended token's rows, or -1
     int defer_stage[NST];
     auto q_rows = [&](int st, const __half *qg) {
       uint8_t *qs = smem + L::kQ + st * kQSlotBytes;
 #pragma unroll
       for (int g = 0; g < G; ++g) bulk_load(qs + g * kQRowBytes, qg + g * a.q_sh, kHeadDim * 2, &full[st]);
     };
+    auto new_rows = [&](int st, int64_t off) {
+      uint8_t *ns = smem + L::kNew + st * 2 * kHeadDim * 2;
+      bulk_load(ns, a.k_new + off, kHeadDim * 2, &full[st]);
+      bulk_load(ns + kHeadDim * 2, a.v_new + off, kHeadDim * 2, &full[st]);
+    };
     auto finish_wait = [&]() {
       asm volatile("griddepcontrol.wait;" ::: "memory");
       waited = true;
-      for (int j = 0; j < ndefer; ++j) q_rows(defer_stage[j], defer_q[j]);
+      for (int j = 0; j < ndefer; ++j) {
+        if (defer_q[j] != nullptr) q_rows(defer_stage[j], defer_q[j]);
+        if (kAppend && defer_new[j] >= 0) new_rows(defer_stage[j], defer_new[j]);
+      }
       ndefer = 0;
     };
     auto emit_range = [&](int u_lo, int u_hi, int owner) {
@@ -277,23 +287,20 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               if (has && i == 0) tx += G * kHeadDim * 2;
               if (app) tx += 2 * kHeadDim * 2;
               mbar_arrive_expect_tx(&full[stage], tx);
-              if (kAppend && app) {
-                uint8_t *ns = smem + L::kNew + stage * 2 * kHeadDim * 2;
-                const int64_t off = pc.b * a.new_sb + pc.kvh * a.new_sh;
-                bulk_load(ns, a.k_new + off, kHeadDim * 2, &full[stage]);
-                bulk_load(ns + kHeadDim * 2, a.v_new + off, kHeadDim * 2, &full[stage]);
+              // q rows (first page of a piece) and the appended token's rows ride
+              // on the stage's barrier; before the wait they are deferred
+              const __half *qg = (has && i == 0) ? a.q + pc.b * a.q_sb + (pc.kvh * G) * a.q_sh : nullptr;
+              const int64_t new_off = (kAppend && app) ? pc.b * a.new_sb + pc.kvh * a.new_sh : -1;
+              if (waited) {
+                if (kAppend && new_off >= 0) new_rows(stage, new_off);
+                if (qg != nullptr) q_rows(stage, qg);
+              } else if (qg != nullptr || new_off >= 0) {
+                defer_q[ndefer] = qg;
+                defer_new[ndefer] = new_off;
+                defer_stage[ndefer] = stage;
+                ++ndefer;
               }
               if (has) {
-                if (i == 0) {  // the piece's q rows ride on its first page's barrier
-                  const __half *qg = a.q + pc.b * a.q_sb + (pc.kvh * G) * a.q_sh;
-                  if (waited) {
-                    q_rows(stage, qg);
-                  } else {
-                    defer_q[ndefer] = qg;
-                    defer_stage[ndefer] = stage;
-                    ++ndefer;
-                  }
-                }
                 uint8_t *dst = smem + stage * L::kStageBytes;
                 const int page = blk * a.hkv + pc.kvh;
                 tma_load_3d(dst, &kmap, &full[stage], 0, 0, page, policy);
@@ -366,8 +373,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       if (hd.nsplit == 1) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
+          const float inv = inv_sum(ls[g]);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) store_out(a, hd.b, h0 + g, lane + 32 * kk, acc[g][kk], ls[g]);
+          for (int kk = 0; kk < 4; ++kk) store_out_inv(a, hd.b, h0 + g, lane + 32 * kk, acc[g][kk], inv);
           if (lane == 0) store_lse(a, hd.b, h0 + g, mx[g], ls[g]);
         }
         continue;

@@ -95,6 +95,11 @@ __device__ __forceinline__ void st_multicast_f16x8(uint4 *p, uint4 v) {
 constexpr int kNvlsUnroll = 4;
 
 __global__ void __launch_bounds__(kNvlsThreads) nvls_allreduce_kernel(const NvlsArgs a) {
+  // Launched as a programmatic dependent: wait for the producer of the partial
+  // (a no-op after a kernel that does not trigger early), then let the next
+  // grid start -- it must itself wait before it reads this kernel's output.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int c = blockIdx.x, tid = threadIdx.x;
   uint32_t *own = a.signals[a.rank];
   __shared__ uint32_t epoch_s;
@@ -176,7 +181,15 @@ extern "C" int b200kv_nvls_allreduce_f16(void *multicast_data, void *const *sign
   a.n = num_elems;
   a.ctas = ctas > 0 ? ctas : 32;
   a.error_flag = error_flag;
-  nvls_allreduce_kernel<<<a.ctas, kNvlsThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  B200KV_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.ctas);
+  cfg.blockDim = dim3(kNvlsThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200KV_CUDA_TRY(cudaLaunchKernelEx(&cfg, nvls_allreduce_kernel, static_cast<const NvlsArgs>(a)));
   return B200KV_OK;
 }

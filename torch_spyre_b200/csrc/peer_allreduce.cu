@@ -119,6 +119,11 @@ __device__ __forceinline__ void add_half8(float (&acc)[8], uint4 x) {
 }
 
 __global__ void __launch_bounds__(kArThreads) peer_allreduce_kernel(const PeerArgs a) {
+  // Launched as a programmatic dependent: wait for the producer of the partial
+  // (a no-op after a kernel that does not trigger early), then let the next
+  // grid start -- it must itself wait before it reads this kernel's output.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int c = blockIdx.x, tid = threadIdx.x;
   const int me = a.rank, N = a.world;
   uint8_t *mine = a.peers[me];
@@ -278,7 +283,15 @@ extern "C" int b200kv_peer_allreduce_f16(void *const *peer_buffers, int32_t rank
   a.lay = peer_layout(capacity_elems, world);
   a.ctas = ctas > 0 ? ctas : 128;
   a.error_flag = error_flag;
-  peer_allreduce_kernel<<<a.ctas, kArThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  B200KV_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.ctas);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B200KV_CUDA_TRY(cudaLaunchKernelEx(&cfg, peer_allreduce_kernel, static_cast<const PeerArgs>(a)));
   return B200KV_OK;
 }

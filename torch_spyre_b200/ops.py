@@ -229,6 +229,7 @@ def _decode_attention_append_op(
     num_splits: int,
     error_flag: Optional[torch.Tensor],
     rope_freqs: Optional[torch.Tensor] = None,
+    inputs_ready: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     _require_cuda(q, k_new, v_new, k_pool, v_pool, block_table, context_lens)
     if q.dim() != 3 or q.dtype != torch.float16 or q.stride(2) != 1:
@@ -252,8 +253,9 @@ def _decode_attention_append_op(
     wbytes = lib.b200kv_decode_workspace_bytes(B, Hq, Hkv, D)
     ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
     rope = () if rope_freqs is None else (_check_rope_freqs(rope_freqs, D, q.device).data_ptr(), rope_freqs.shape[0])
-    _lib.call(
-        "b200kv_decode_attention_append_rope_f16" if rope else "b200kv_decode_attention_append_f16",
+    if rope and inputs_ready:
+        raise ValueError("inputs_ready is not offered with rope_freqs")
+    args = (
         q.data_ptr(), q.stride(0), q.stride(1),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), k_new.stride(1),
         k_pool.data_ptr(), v_pool.data_ptr(), *rope,
@@ -264,14 +266,21 @@ def _decode_attention_append_op(
         B, Hq, Hkv, D, NB, block_table.shape[1],
         float(scale), int(num_splits),
         ws.data_ptr(), ws.numel(),
-        _ptr(error_flag), _stream_ptr(q.device),
+        _ptr(error_flag),
     )
+    if rope:
+        _lib.call("b200kv_decode_attention_append_rope_f16", *args, _stream_ptr(q.device))
+    elif inputs_ready:
+        _lib.call("b200kv_decode_attention_append_ex_f16", *args, DECODE_INPUTS_READY, _stream_ptr(q.device))
+    else:
+        _lib.call("b200kv_decode_attention_append_f16", *args, _stream_ptr(q.device))
     _maybe_check_flag(error_flag, "decode_attention_append")
     return out, lse
 
 
 @_decode_attention_append_op.register_fake
-def _(q, k_new, v_new, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag, rope_freqs=None):
+def _(q, k_new, v_new, k_pool, v_pool, block_table, context_lens, scale, num_splits, error_flag, rope_freqs=None,
+      inputs_ready=False):
     B, Hq, D = q.shape
     return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)
 
@@ -291,9 +300,16 @@ def decode_attention_append(
     k_scale: Optional[torch.Tensor] = None,
     v_scale: Optional[torch.Tensor] = None,
     rope_freqs: Optional[torch.Tensor] = None,
+    inputs_ready: bool = False,
 ):
     """Appends the new token's K/V rows ([B, Hkv, D], at position
     context_lens[b] - 1) to the pools and decodes, in one launch.
+
+    ``inputs_ready`` (fp16 pools, no rope): the caller vouches that the pools
+    (other than the rows appended here), block table and context lengths were
+    written before the preceding kernel on the stream began, so the kernel
+    starts its page loads while that kernel finishes; q and the new rows may be
+    written by it.
 
     Same result as ``kv_append`` at those slots followed by
     ``decode_attention`` (the HF ``index_copy_`` + SDPA step of the reference).
@@ -315,7 +331,7 @@ def decode_attention_append(
     else:
         out, lse = torch.ops.b200kv.decode_attention_append(
             q, k_new, v_new, k_pool, v_pool, block_table, context_lens, float(scale), int(num_splits), error_flag,
-            rope_freqs
+            rope_freqs, bool(inputs_ready)
         )
     return (out, lse) if return_lse else out
 

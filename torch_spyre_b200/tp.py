@@ -302,8 +302,9 @@ def tp_decode_step(
     attn_fn: Optional[AttnFn] = None,
     k_scale: Optional[torch.Tensor] = None,
     v_scale: Optional[torch.Tensor] = None,
-    allreduce: Optional[PeerAllReduce] = None,
+    allreduce=None,
     fused_oproj: bool = False,
+    inputs_ready: bool = False,
 ) -> torch.Tensor:
     """One rank's step: local decode -> o_proj partial -> SUM all-reduce.
 
@@ -314,12 +315,18 @@ def tp_decode_step(
     the next step) or, with ``fused_oproj``, the o_proj GEMM and the
     all-reduce run as one kernel (``PeerAllReduce.oproj_all_reduce``);
     otherwise NCCL (``group``) reduces it.
+    ``inputs_ready``: the pools, block table and context lengths were written
+    before the preceding kernel on the stream began (see
+    ``decode_attention``), so the decode may start its page loads while that
+    kernel -- e.g. the previous step's all-reduce -- finishes.
     Every rank must call this in the same order (it contains one collective).
     """
     if attn_fn is None:
         from .ops import decode_attention as attn_fn
     if k_scale is not None:
         attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens, k_scale=k_scale, v_scale=v_scale)
+    elif inputs_ready:
+        attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens, inputs_ready=True)
     else:
         attn = attn_fn(q_local, k_pool, v_pool, block_table, context_lens)
     B = attn.shape[0]
