@@ -572,15 +572,17 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         data = sum(t.numel() * t.element_size() for t in parts.values())
         return host, dev, views, h_out, data
 
-    staged = [pack(s) for s in sets]
+    n_sets = len(sets)
+    # one staging buffer per step of a captured graph (tp70b: per input set)
+    pipe_steps = n_sets if tp else n_sets * max(1, 16 // n_sets)
+    staged = [pack(sets[k % n_sets]) for k in range(pipe_steps)]
     B = sets[0].q.shape[0]
     h2d = int(statistics.mean(x[4] for x in staged))
     d2h = staged[0][3].numel() * 2
-    n_sets = len(sets)
     n = n_sets * max(1, -(-max(3, min(steps, 500)) // n_sets))
 
     def compute(i):
-        s = sets[i]
+        s = sets[i % n_sets]
         v = staged[i][2]
         if tp:
             from torch_spyre_b200.tp import HeadShard, tp_decode_step
@@ -605,7 +607,44 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
 
     up_stream, down_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
-    pipe_rounds = max(1, -(-8 // n_sets))  # rounds of n_sets steps per captured graph
+    pipe_rounds = max(1, -(-8 // n_sets))  # rounds of n_sets steps per captured graph (tp70b)
+    group = 4  # steps per wait on the copy streams
+
+    def pipelined_steps():
+        # the serving pipeline of the decode workloads: every step's inputs
+        # cross in their own H2D copy and its output in its own D2H copy, on
+        # two copy streams, while the steps' kernels run back to back.  The
+        # uploads run ahead of the kernels (the whole graph's steps' inputs are
+        # staged at once), and the compute stream waits on the upload stream
+        # once per group of 4 steps (the downloads are forked once per group):
+        # a kernel that waits on a copy cannot start under its predecessor
+        # (programmatic dependent launch applies between kernels only), which
+        # costs ~7 us per waiting kernel on B200.
+        cur = torch.cuda.current_stream(device)
+        up_stream.wait_stream(cur)
+        down_stream.wait_stream(cur)
+        landed = []
+        with torch.cuda.stream(up_stream):
+            for k in range(pipe_steps):
+                staged[k][1].copy_(staged[k][0], non_blocking=True)
+                if k % group == group - 1 or k == pipe_steps - 1:
+                    ev = torch.cuda.Event()
+                    ev.record(up_stream)
+                    landed.append(ev)
+        outs = []
+        for k in range(pipe_steps):
+            if k % group == 0:
+                cur.wait_event(landed[k // group])
+            outs.append(compute(k))
+            if k % group == group - 1 or k == pipe_steps - 1:
+                done = torch.cuda.Event()
+                done.record(cur)
+                with torch.cuda.stream(down_stream):
+                    down_stream.wait_event(done)
+                    for j in range(k - k % group, k + 1):
+                        staged[j][3].copy_(outs[j], non_blocking=True)
+        cur.wait_stream(up_stream)
+        cur.wait_stream(down_stream)
 
     def pipelined_rounds():
         # the serving pipeline: every step's inputs go up on a copy stream and
@@ -665,18 +704,26 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         with torch.cuda.stream(stream):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                pipelined_rounds()
-        graph_ms = timed(g.replay, n_sets * pipe_rounds)
+                if tp:
+                    pipelined_rounds()
+                else:
+                    pipelined_steps()
+        per_replay = n_sets * pipe_rounds if tp else pipe_steps
+        graph_ms = timed(g.replay, per_replay)
     ms = graph_ms if graph_ms is not None else eager_ms
     tokens = B if tp else B * world
     return {"value": round(tokens / (ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "steps": (max(1, n // (n_sets * pipe_rounds)) * n_sets * pipe_rounds if graph_ms is not None
+            "steps": (max(1, n // per_replay) * per_replay if graph_ms is not None
                       else max(1, n // n_sets) * n_sets),
             "ms_per_step": round(ms, 5),
             "path": ("torch.ops.b200kv.decode_attention_append (tp70b: kv_append + decode_attention + o_proj"
-                     " + all-reduce) with pinned host buffers, "
-                     + ("captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
+                     " + all-reduce) with pinned host buffers, one H2D copy of each step's inputs and one D2H "
+                     "copy of its output, "
+                     + (("captured in a CUDA graph of 16 steps and replayed; the copies run on two copy streams, "
+                         "the uploads ahead of the kernels, the compute stream waiting on them once per 4 steps")
+                        if graph_ms is not None and not tp else
+                        "captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
                         "overlapping the neighbouring steps' compute" if graph_ms is not None
                         else "eager")),
             "eager": {"value": round(tokens / (eager_ms / 1e3), 1), "ms_per_step": round(eager_ms, 5)},
