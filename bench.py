@@ -918,8 +918,17 @@ def run_tp_block(args, rank, world, local, device):
     dec_bytes = statistics.mean(s.step_bytes for s in sets)
     dec_traffic, dec_traffic_src = profiled_traffic("decode_kernel", f"tp70b_kv{cfg.num_kv_heads // world}"
                                                     if world > 1 else "tp70b", dec_bytes)
+    # the default all-reduce of the step: the NVLink SHARP kernel from N = 4 on
+    # (where its in-switch reduction moves fewer bytes than the packet
+    # two-shot), the peer-memory kernel below that or without multicast
+    default_nvls = nvls_step_us is not None and world >= 4
+    best_us = nvls_step_us if default_nvls else step_us
+    res["allreduce"] = ("NVLink SHARP kernel (multimem)" if default_nvls
+                        else "peer-memory kernel" if world > 1 else "none (N = 1)")
     res.update({
-        "value": round(B / (step_us / 1e6), 1), "unit": "tokens/s", "ms_per_step": round(step_us / 1e3, 5),
+        "value": round(B / (best_us / 1e6), 1), "unit": "tokens/s", "ms_per_step": round(best_us / 1e3, 5),
+        "value_peer": round(B / (step_us / 1e6), 1) if world > 1 else None,
+        "ms_per_step_peer": round(step_us / 1e3, 5) if world > 1 else None,
         "value_fused": round(B / (fused_us / 1e6), 1) if fused_us else None,
         "ms_per_step_fused": round(fused_us / 1e3, 5) if fused_us else None,
         "decode_us": round(dec_us, 2),
