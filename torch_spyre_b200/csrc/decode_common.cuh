@@ -363,10 +363,25 @@ __device__ __forceinline__ void store_out(const DecodeArgs &a, int b, int h, int
                                           float l) {
   a.out[b * a.o_sb + h * a.o_sh + d] = __float2half_rn(l > 0.f ? acc / l : 0.f);
 }
-// The same with the reciprocal of the sum (one division per head).
+// The reciprocal of a head's sum (one division per head, applied by store_out4_inv).
 __device__ __forceinline__ float inv_sum(float l) { return l > 0.f ? __frcp_rn(l) : 0.f; }
-__device__ __forceinline__ void store_out_inv(const DecodeArgs &a, int b, int h, int d, float acc, float inv) {
-  a.out[b * a.o_sb + h * a.o_sh + d] = __float2half_rn(__fmul_rn(acc, inv));
+// Dims d0..d0+3 of (b, head h) from unnormalised accumulators: one 8-byte
+// store where the output row allows it, else four 2-byte stores (the values
+// are the same either way).
+__device__ __forceinline__ void store_out4_inv(const DecodeArgs &a, int b, int h, int d0, const float (&acc)[4],
+                                               float inv) {
+  __half *p = a.out + b * a.o_sb + h * a.o_sh + d0;
+  const __half2 lo = __floats2half2_rn(__fmul_rn(acc[0], inv), __fmul_rn(acc[1], inv));
+  const __half2 hi = __floats2half2_rn(__fmul_rn(acc[2], inv), __fmul_rn(acc[3], inv));
+  if ((reinterpret_cast<uintptr_t>(p) & 7u) == 0) {
+    *reinterpret_cast<uint2 *>(p) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+  } else {
+    p[0] = __low2half(lo);
+    p[1] = __high2half(lo);
+    p[2] = __low2half(hi);
+    p[3] = __high2half(hi);
+  }
 }
 __device__ __forceinline__ void store_lse(const DecodeArgs &a, int b, int h, float m, float l) {
   if (a.lse)
@@ -397,7 +412,8 @@ __device__ __forceinline__ void combine_partials(const DecodeArgs &a, const Item
 }
 
 // Log-sum-exp merge of a pair's split partials by one warp: lane l produces
-// output dims l, l + 32, l + 64, l + 96 of every head of the pair.  Splits are
+// output dims 4l .. 4l + 3 of every head of the pair (one 16-byte load per
+// partial row, one 8-byte store per output row).  Splits are
 // read two at a time (every load of a batch issued before any is used) and
 // folded into a running (max, sum, accumulator) per head, so any number of
 // splits merges without shared memory.  The running state starts from
@@ -419,9 +435,12 @@ __device__ __forceinline__ void combine_online_warp_from(const DecodeArgs &a, in
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         ml[j][g] = in ? __ldcg(a.part_ml + slot * G + g) : make_float2(-CUDART_INF_F, 0.f);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ov[j][g][k] = in ? __ldcg(a.part_o + (slot * G + g) * kHeadDim + lane + 32 * k) : 0.f;
+        const float4 v = in ? __ldcg(reinterpret_cast<const float4 *>(a.part_o + (slot * G + g) * kHeadDim) + lane)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        ov[j][g][0] = v.x;
+        ov[j][g][1] = v.y;
+        ov[j][g][2] = v.z;
+        ov[j][g][3] = v.w;
       }
     }
 #pragma unroll
@@ -444,9 +463,7 @@ __device__ __forceinline__ void combine_online_warp_from(const DecodeArgs &a, in
   const int h0 = kvh * G;
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const float inv = inv_sum(Ls[g]);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) store_out_inv(a, b, h0 + g, lane + 32 * k, acc[g][k], inv);
+    store_out4_inv(a, b, h0 + g, 4 * lane, acc[g], inv_sum(Ls[g]));
     if (lane == 0) store_lse(a, b, h0 + g, M[g], Ls[g]);
   }
 }

@@ -75,13 +75,17 @@ constexpr int kQRowBytes = 272;
 constexpr int kQSlotBytes = 8 * kQRowBytes;
 
 // Hand-off of a finished piece from the consumer warps to the epilogue warp:
-// every warp's unnormalised O^T [128 d][8 h], its (max, sum) per head and the
-// piece's identity.  Two buffers let the consumers run a piece ahead.
+// every warp's unnormalised output rows O [8 h][128 d], its (max, sum) per
+// head and the piece's identity.  Two buffers let the consumers run a piece
+// ahead.  Rows are padded to 132 floats: the consumers' scalar writes (lanes
+// of 8 dims x 4 head pairs) fall in 32 distinct banks, and the epilogue reads
+// 4 consecutive dims per lane with one conflict-free 16-byte load.
 struct PieceHeader {
   int b, kvh, pair, nsplit, slot, end, tail, own_first;
 };
-constexpr int kPieceO = 0;                                   // float [4][128][8]
-constexpr int kPieceML = kConsumerWarps * kHeadDim * 8 * 4;  // float2 [4][8]
+constexpr int kPieceRow = kHeadDim + 4;
+constexpr int kPieceO = 0;                                    // float [4][8][kPieceRow]
+constexpr int kPieceML = kConsumerWarps * 8 * kPieceRow * 4;  // float2 [4][8]
 constexpr int kPieceHdr = kPieceML + kConsumerWarps * 8 * 8;
 constexpr int kPieceBytes = (kPieceHdr + 64 + 127) & ~127;
 constexpr int kPieceBufs = 2;
@@ -224,13 +228,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const uint64_t policy = l2_policy_evict_first();
     int stage = 0;
     uint32_t phase = 0;
-    // early start: stages issued before griddepcontrol.wait get their q rows
-    // after it (their full barriers already expect those bytes)
+    // early start: the stages issued before griddepcontrol.wait -- stages
+    // 0 .. issued - 1, at most one trip round the ring -- get their q rows and
+    // appended rows after it (their full barriers already expect those bytes;
+    // their descriptors stay in place until those bytes land)
     bool waited = !early;
-    int issued = 0, ndefer = 0;
-    const __half *defer_q[NST];
-    int64_t defer_new[NST];  // offset of the appended token's rows, or -1
-    int defer_stage[NST];
+    int issued = 0;
     auto q_rows = [&](int st, const __half *qg) {
       uint8_t *qs = smem + L::kQ + st * kQSlotBytes;
 #pragma unroll
@@ -244,11 +247,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     auto finish_wait = [&]() {
       asm volatile("griddepcontrol.wait;" ::: "memory");
       waited = true;
-      for (int j = 0; j < ndefer; ++j) {
-        if (defer_q[j] != nullptr) q_rows(defer_stage[j], defer_q[j]);
-        if (kAppend && defer_new[j] >= 0) new_rows(defer_stage[j], defer_new[j]);
+      for (int st = 0; st < issued; ++st) {
+        const StageDesc &d = descs[st];
+        if (kAppend && (d.flags & kDescNew)) new_rows(st, d.b * a.new_sb + d.kvh * a.new_sh);
+        if ((d.flags & (kDescFirst | kDescPage)) == (kDescFirst | kDescPage))
+          q_rows(st, a.q + d.b * a.q_sb + (d.kvh * G) * a.q_sh);
       }
-      ndefer = 0;
     };
     auto emit_range = [&](int u_lo, int u_hi, int owner) {
       for (int u = u_lo; u < u_hi;) {
@@ -289,16 +293,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
               mbar_arrive_expect_tx(&full[stage], tx);
               // q rows (first page of a piece) and the appended token's rows ride
               // on the stage's barrier; before the wait they are deferred
-              const __half *qg = (has && i == 0) ? a.q + pc.b * a.q_sb + (pc.kvh * G) * a.q_sh : nullptr;
-              const int64_t new_off = (kAppend && app) ? pc.b * a.new_sb + pc.kvh * a.new_sh : -1;
               if (waited) {
-                if (kAppend && new_off >= 0) new_rows(stage, new_off);
-                if (qg != nullptr) q_rows(stage, qg);
-              } else if (qg != nullptr || new_off >= 0) {
-                defer_q[ndefer] = qg;
-                defer_new[ndefer] = new_off;
-                defer_stage[ndefer] = stage;
-                ++ndefer;
+                if (kAppend && app) new_rows(stage, pc.b * a.new_sb + pc.kvh * a.new_sh);
+                if (has && i == 0) q_rows(stage, a.q + pc.b * a.q_sb + (pc.kvh * G) * a.q_sh);
               }
               if (has) {
                 uint8_t *dst = smem + stage * L::kStageBytes;
@@ -343,27 +340,27 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       if (hd.end) break;
       const float *wo = reinterpret_cast<const float *>(buf + kPieceO);
       const float2 *wml = reinterpret_cast<const float2 *>(buf + kPieceML);
+      // lane l holds dims 4l .. 4l + 3 of every head
       float acc[G][4], mx[G], ls[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         float m = -CUDART_INF_F;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) m = fmaxf(m, wml[w * 8 + g].x);
-        float l = 0.f, sw[kConsumerWarps];
+        float l = 0.f, x[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) {
           const float2 ml = wml[w * 8 + g];
-          sw[w] = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - m);
-          l = fmaf(ml.y, sw[w], l);
+          const float sw = ml.x == -CUDART_INF_F ? 0.f : exp2f(ml.x - m);
+          l = fmaf(ml.y, sw, l);
+          const float4 v = reinterpret_cast<const float4 *>(wo + (w * 8 + g) * kPieceRow)[lane];
+          x[0] = fmaf(v.x, sw, x[0]);
+          x[1] = fmaf(v.y, sw, x[1]);
+          x[2] = fmaf(v.z, sw, x[2]);
+          x[3] = fmaf(v.w, sw, x[3]);
         }
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          float x = 0.f;
-#pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w)
-            x = fmaf(wo[(w * kHeadDim + lane + 32 * kk) * 8 + g], sw[w], x);
-          acc[g][kk] = kFp8 ? x * vsc : x;
-        }
+        for (int kk = 0; kk < 4; ++kk) acc[g][kk] = kFp8 ? x[kk] * vsc : x[kk];
         mx[g] = m;
         ls[g] = l;
       }
@@ -373,9 +370,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       if (hd.nsplit == 1) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const float inv = inv_sum(ls[g]);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) store_out_inv(a, hd.b, h0 + g, lane + 32 * kk, acc[g][kk], inv);
+          store_out4_inv(a, hd.b, h0 + g, 4 * lane, acc[g], inv_sum(ls[g]));
           if (lane == 0) store_lse(a, hd.b, h0 + g, mx[g], ls[g]);
         }
         continue;
@@ -402,8 +397,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       float *po = a.part_o + static_cast<int64_t>(hd.slot) * G * kHeadDim;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) __stcg(po + g * kHeadDim + lane + 32 * kk, acc[g][kk]);
+        __stcg(reinterpret_cast<float4 *>(po + g * kHeadDim) + lane,
+               make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]));
         if (lane == 0) __stcg(a.part_ml + static_cast<int64_t>(hd.slot) * G + g, make_float2(mx[g], ls[g]));
       }
       __syncwarp();  // the warp's partial stores precede lane 0's release
@@ -474,13 +469,17 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         wml[warp * 8 + hc + 1] = make_float2(m1, l1);
       }
       // accumulator rows of m-tile mt: d = 16 mt + r and + 8 (fp16 pages),
-      // d = 16 mt + 2r and + 1 (fp8 pages), r = lane / 4
+      // d = 16 mt + 2r and + 1 (fp8 pages), r = lane / 4; columns: heads hc, hc + 1
+      float *w0 = wo + (warp * 8 + hc) * kPieceRow;
+      float *w1 = w0 + kPieceRow;
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         const int dd = mt * 16 + (kFp8 ? 2 * (lane >> 2) : (lane >> 2));
-        float *w = wo + (warp * kHeadDim + dd) * 8 + hc;
-        *reinterpret_cast<float2 *>(w) = make_float2(o[mt][0], o[mt][1]);
-        *reinterpret_cast<float2 *>(w + (kFp8 ? 8 : 8 * 8)) = make_float2(o[mt][2], o[mt][3]);
+        const int d2 = dd + (kFp8 ? 1 : 8);
+        w0[dd] = o[mt][0];
+        w1[dd] = o[mt][1];
+        w0[d2] = o[mt][2];
+        w1[d2] = o[mt][3];
       }
     }
     if (warp == 0 && lane == 0) {
