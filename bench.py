@@ -883,8 +883,9 @@ def run_tp_block(args, rank, world, local, device):
                     if fused_ok else None)
         nvls_step_us = (_graph_us([lambda s=s: step(s, reducer=nv) for s in sets], stream, world, n_steps)
                         if nv is not None else None)
+        # the decode alone, launched as in the step (early start)
         dec_us = _graph_us([lambda s=s: tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table,
-                                                             s.context_lens) for s in sets],
+                                                             s.context_lens, inputs_ready=True) for s in sets],
                            stream, world, n_steps)
         oproj_us = _graph_us([lambda w=w: torch.matmul(attn, w.t(), out=partial) for w in w_rot],
                              stream, world, TP_COMPONENT_LAUNCHES)

@@ -9,7 +9,7 @@
 // in the n = 8 dimension (G < 8 is zero-padded), which leaves the SMs almost
 // idle and the kernel bound by HBM.
 //
-// CTA = 1 producer warp + 4 consumer warps + 1 epilogue warp, one CTA per SM
+// CTA = 1 producer warp + 4 consumer warps + 2 epilogue warps, one CTA per SM
 // (persistent).  Work partition: the balanced unit split of decode_common.cuh
 // (every CTA streams the same number of pages; a sequence-head cut by a CTA
 // boundary is a split).
@@ -36,7 +36,10 @@
 //   epilogue  merges the 4 warps' states of a finished piece, writes the fp16
 //             output (unsplit pair) or the fp32 partial, takes the pair's
 //             completion ticket and, holding the last one, merges the pair's
-//             partials (online log-sum-exp, decode_common.cuh).
+//             partials (online log-sum-exp, decode_common.cuh).  Two epilogue
+//             warps take the pieces in turn (warp e owns piece buffer e), so a
+//             piece whose merge waits on L2 round trips does not hold up the
+//             next one -- the CTA's final piece in particular.
 //
 // Fused append (kAppend) may also apply the rotary embedding (rope.cuh) of
 // position context_len - 1 to q and to the new K row: q in its MMA fragments
@@ -65,21 +68,23 @@ namespace {
 
 constexpr int kConsumerWarps = 4;
 
+constexpr int kEpilogueWarps = 2;
 constexpr int kProducerWarp = kConsumerWarps;      // warp 4
-constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warp 5
-constexpr int kMmaThreads = (kConsumerWarps + 2) * 32;
+constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warps 5, 6
+constexpr int kMmaThreads = (kConsumerWarps + 1 + kEpilogueWarps) * 32;
 
 // Staged q of one piece: G rows of 128 fp16, row stride padded to 272 B so
 // the Q^T fragment loads (8 heads x 4 lanes) hit 32 distinct banks.
 constexpr int kQRowBytes = 272;
 constexpr int kQSlotBytes = 8 * kQRowBytes;
 
-// Hand-off of a finished piece from the consumer warps to the epilogue warp:
+// Hand-off of a finished piece from the consumer warps to an epilogue warp:
 // every warp's unnormalised output rows O [8 h][128 d], its (max, sum) per
-// head and the piece's identity.  Two buffers let the consumers run a piece
-// ahead.  Rows are padded to 132 floats: the consumers' scalar writes (lanes
-// of 8 dims x 4 head pairs) fall in 32 distinct banks, and the epilogue reads
-// 4 consecutive dims per lane with one conflict-free 16-byte load.
+// head and the piece's identity.  Piece k goes to buffer k & 1, which
+// epilogue warp k & 1 drains.  Rows are padded to 132 floats: the consumers'
+// scalar writes (lanes of 8 dims x 4 head pairs) fall in 32 distinct banks,
+// and the epilogue reads 4 consecutive dims per lane with one conflict-free
+// 16-byte load.
 struct PieceHeader {
   int b, kvh, pair, nsplit, slot, end, tail, own_first;
 };
@@ -88,7 +93,7 @@ constexpr int kPieceO = 0;                                    // float [4][8][kP
 constexpr int kPieceML = kConsumerWarps * 8 * kPieceRow * 4;  // float2 [4][8]
 constexpr int kPieceHdr = kPieceML + kConsumerWarps * 8 * 8;
 constexpr int kPieceBytes = (kPieceHdr + 64 + 127) & ~127;
-constexpr int kPieceBufs = 2;
+constexpr int kPieceBufs = kEpilogueWarps;
 
 template <int NST, bool kFp8>
 struct MmaSmem {
@@ -327,14 +332,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   // Takes finished pieces from the consumers: merges the 4 warps' states,
   // writes the fp16 output (single piece) or the fp32 partial, takes the
   // pair's completion ticket and, holding the last one, merges the pair's
-  // partials.  Runs beside the consumers, which never wait for it unless it
-  // falls two pieces behind.
+  // partials.  Epilogue warp e takes pieces e, e + 2, e + 4, ... from buffer
+  // e.  Runs beside the consumers, which never wait for it unless a warp
+  // falls a whole piece behind.
   if (early) asm volatile("griddepcontrol.wait;" ::: "memory");  // consumers and epilogue
-  if (warp == kEpilogueWarp) {
+  if (warp >= kEpilogueWarp) {
     const float vsc = kFp8 ? __half2float(*a.v_scale) : 1.f;  // V dequantisation scale
-    for (int k = 0;; ++k) {
-      const int pb = k & 1;
-      mbar_wait_bounded(&pfull[pb], (k >> 1) & 1, a.error_flag);
+    const int pb = warp - kEpilogueWarp;
+    for (uint32_t j = 0;; ++j) {
+      mbar_wait_bounded(&pfull[pb], j & 1u, a.error_flag);
       const uint8_t *buf = smem + L::kPiece + pb * kPieceBytes;
       const PieceHeader hd = *reinterpret_cast<const PieceHeader *>(buf + kPieceHdr);
       if (hd.end) break;
@@ -454,8 +460,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
   }
 
-  // Hands this warp's state of the finished piece (or the end marker) to the
-  // epilogue through piece buffer k & 1.
+  // Hands this warp's state of the finished piece (or an end marker) to
+  // epilogue warp k & 1 through piece buffer k & 1.
   auto hand_off = [&](int k, const StageDesc &d, bool end, const float (&o)[8][4], float m0,
                       float m1, float l0, float l1) {
     const int pb = k & 1;
@@ -565,8 +571,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   for (;; ++seq) {
     mbar_wait_bounded(&full[stage], phase, a.error_flag);
     const StageDesc d = descs[stage];
-    if (d.flags & kDescEnd) {
+    if (d.flags & kDescEnd) {  // one end marker per epilogue warp
       hand_off(piece, d, true, o, m0, m1, l0, l1);
+      hand_off(piece + 1, d, true, o, m0, m1, l0, l1);
       break;
     }
     const bool first = d.flags & kDescFirst, last = d.flags & kDescLast;
