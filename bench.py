@@ -350,14 +350,6 @@ def run_ours(args, rank, world, local):
         from torch_spyre_b200.tp import PeerAllReduce
 
         ar = PeerAllReduce(B * cfg.hidden, device=device)
-    nv = None
-    if world > 1:  # the NVLink SHARP all-reduce, where the GPUs offer multicast (decided collectively)
-        from torch_spyre_b200.tp import NvlsAllReduce
-
-        try:
-            nv = NvlsAllReduce(B * cfg.hidden, device=device)
-        except RuntimeError:
-            nv = None
 
     def step(s):
         if tp:
@@ -765,7 +757,7 @@ def _graph_us(fns, stream, world, launches):
     return max_over_ranks(us, world)
 
 
-def tp_parity_check(rank, world, device, ar, fused_ok, nv=None):
+def tp_parity_check(rank, world, device, ar, fused_ok, nv=None, nv_ll=None):
     """Checker, run after the timed region: one small head-sharded step (ragged
     contexts, partial pages) through each path the block times, against the
     CPU oracle (the reference's CPU eager decode of all heads, then the full
@@ -791,6 +783,8 @@ def tp_parity_check(rank, world, device, ar, fused_ok, nv=None):
             ys["fused"] = tp_decode_step(*step_args, allreduce=ar, fused_oproj=True).clone()
         if nv is not None:
             ys["nvls"] = tp_decode_step(*step_args, allreduce=nv).clone()
+        if nv_ll is not None:
+            ys["nvls_ll"] = tp_decode_step(*step_args, allreduce=nv_ll).clone()
         ys["nccl"] = tp_decode_step(*step_args)
     torch.cuda.synchronize(device)
     ref = tp_step_cpu(full.q, full.k_pool, full.v_pool, full.block_table, full.context_lens, w_o)
@@ -799,7 +793,7 @@ def tp_parity_check(rank, world, device, ar, fused_ok, nv=None):
         y = y.cpu().float()
         ok &= bool(torch.allclose(y, ref, atol=TP_ATOL, rtol=TP_RTOL))
         err = max(err, float((y - ref).abs().max()))
-    for x in (ar, nv):
+    for x in (ar, nv, nv_ll):
         if x is not None:
             ok &= int(x.error_flag.item()) == 0
     flag = -max_over_ranks(-float(ok), world)  # min over ranks
@@ -843,9 +837,10 @@ def run_tp_block(args, rank, world, local, device):
         from torch_spyre_b200.tp import NvlsAllReduce
 
         try:
-            nv = NvlsAllReduce(B * cfg.hidden, device=device)
+            nv = NvlsAllReduce(B * cfg.hidden, device=device, low_latency=False)
         except RuntimeError:
             nv = None
+    nv_ll = NvlsAllReduce(B * cfg.hidden, device=device, low_latency=True) if nv is not None else None
     # the fused kernel needs hidden / (64 N) whole tiles and 128 co-resident CTAs
     fused_ok = cfg.hidden % (64 * world) == 0 and B <= 128
     partial = torch.empty((B, cfg.hidden), dtype=torch.float16, device=device)
@@ -869,6 +864,7 @@ def run_tp_block(args, rank, world, local, device):
                 step(s, fused=True)
             if nv is not None:
                 step(s, reducer=nv)
+                step(s, reducer=nv_ll)
         stream.synchronize()
     barrier(world)
     reps = max(1, -(-TP_STEPS // n_sets))
@@ -883,6 +879,8 @@ def run_tp_block(args, rank, world, local, device):
                     if fused_ok else None)
         nvls_step_us = (_graph_us([lambda s=s: step(s, reducer=nv) for s in sets], stream, world, n_steps)
                         if nv is not None else None)
+        nvls_ll_step_us = (_graph_us([lambda s=s: step(s, reducer=nv_ll) for s in sets], stream, world, n_steps)
+                           if nv_ll is not None else None)
         # the decode alone, launched as in the step (early start)
         dec_us = _graph_us([lambda s=s: tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table,
                                                              s.context_lens, inputs_ready=True) for s in sets],
@@ -891,7 +889,7 @@ def run_tp_block(args, rank, world, local, device):
                              stream, world, TP_COMPONENT_LAUNCHES)
         fused_alone_us = (_graph_us([lambda w=w: ar.oproj_all_reduce(attn, w, out=partial) for w in w_rot],
                                     stream, world, TP_COMPONENT_LAUNCHES) if fused_ok else None)
-        ar_us = nccl_us = nvls_us = None
+        ar_us = nccl_us = nvls_us = nvls_ll_us = None
         if world > 1:
             buf = ar.buffer((B, cfg.hidden))
             buf.zero_()
@@ -900,6 +898,9 @@ def run_tp_block(args, rank, world, local, device):
                 nbuf_mc = nv.buffer((B, cfg.hidden))
                 nbuf_mc.zero_()
                 nvls_us = _graph_us([lambda: nv.all_reduce(nbuf_mc)], stream, world, TP_COMPONENT_LAUNCHES)
+                lbuf = nv_ll.buffer((B, cfg.hidden))
+                lbuf.zero_()
+                nvls_ll_us = _graph_us([lambda: nv_ll.all_reduce(lbuf)], stream, world, TP_COMPONENT_LAUNCHES)
             import torch.distributed as dist
 
             nbuf = torch.zeros((B, cfg.hidden), dtype=torch.float16, device=device)
@@ -919,12 +920,12 @@ def run_tp_block(args, rank, world, local, device):
     dec_bytes = statistics.mean(s.step_bytes for s in sets)
     dec_traffic, dec_traffic_src = profiled_traffic("decode_kernel", f"tp70b_kv{cfg.num_kv_heads // world}"
                                                     if world > 1 else "tp70b", dec_bytes)
-    # the default all-reduce of the step: the NVLink SHARP kernel from N = 4 on
-    # (where its in-switch reduction moves fewer bytes than the packet
-    # two-shot), the peer-memory kernel below that or without multicast
-    default_nvls = nvls_step_us is not None and world >= 4
-    best_us = nvls_step_us if default_nvls else step_us
-    res["allreduce"] = ("NVLink SHARP kernel (multimem)" if default_nvls
+    # the default all-reduce of the step: the low-latency kernel (peer stores,
+    # then one multicast store, flags in the data) wherever the GPUs offer
+    # NVLink multicast, the peer-memory packet kernel without it
+    default_ll = nvls_ll_step_us is not None
+    best_us = nvls_ll_step_us if default_ll else step_us
+    res["allreduce"] = ("low-latency kernel (peer stores + multimem.st, no barrier)" if default_ll
                         else "peer-memory kernel" if world > 1 else "none (N = 1)")
     res.update({
         "value": round(B / (best_us / 1e6), 1), "unit": "tokens/s", "ms_per_step": round(best_us / 1e3, 5),
@@ -942,17 +943,21 @@ def run_tp_block(args, rank, world, local, device):
         "allreduce_nvls_us": round(nvls_us, 2) if nvls_us else None,
         "value_nvls": round(B / (nvls_step_us / 1e6), 1) if nvls_step_us else None,
         "ms_per_step_nvls": round(nvls_step_us / 1e3, 5) if nvls_step_us else None,
+        "allreduce_nvls_ll_us": round(nvls_ll_us, 2) if nvls_ll_us else None,
+        "value_nvls_ll": round(B / (nvls_ll_step_us / 1e6), 1) if nvls_ll_step_us else None,
+        "ms_per_step_nvls_ll": round(nvls_ll_step_us / 1e3, 5) if nvls_ll_step_us else None,
         "allreduce_nccl_us": round(nccl_us, 2) if nccl_us else None,
         "gpu_launches": res["steps"] * (2 if world > 1 else 1),
         "clocks": clk.summary(),
     })
-    ok, err, paths = tp_parity_check(rank, world, device, ar if world > 1 else None, fused_ok, nv)
+    ok, err, paths = tp_parity_check(rank, world, device, ar if world > 1 else None, fused_ok, nv, nv_ll)
     res.update({"tp_parity_ok": ok, "tp_parity_max_abs_err": round(err, 6), "tp_parity_paths": paths,
                 "tp_parity_case": f"B={len(TP_PARITY_CTX)} ctx {TP_PARITY_CTX}, all heads, hidden {cfg.hidden}, "
                                   f"vs CPU oracle (decode x W_o in fp32), atol {TP_ATOL} rtol {TP_RTOL}"})
     del w_rot
     if nv is not None:
         nv.close()
+        nv_ll.close()
     ar.close()
     return res
 

@@ -499,7 +499,7 @@ B200KV_API int b200kv_peer_allreduce_f16(void *const *peer_buffers, int32_t rank
  * separate zero-initialised signal area of b200kv_nvls_signal_bytes() per
  * rank, mapped into every rank (table of all ranks' areas, own included, in
  * rank order, 256-byte aligned).  num_elems must be a multiple of 8 * world;
- * ctas in [0, 64] (0 = 32).  The data buffer holds the partial on entry and
+ * ctas in [0, 256] (0 = 32).  The data buffer holds the partial on entry and
  * the sum on exit.  Every rank must make the same calls in the same order;
  * waits are bounded (2 s, then B200KV_DEVERR_TIMEOUT in error_flag and the
  * output is undefined).  Calls replay correctly from CUDA graphs.
@@ -508,6 +508,31 @@ B200KV_API int64_t b200kv_nvls_signal_bytes(void);
 B200KV_API int b200kv_nvls_allreduce_f16(void *multicast_data, void *const *signal_areas,
                                          int32_t rank, int32_t world, int64_t num_elems,
                                          int32_t ctas, int32_t *error_flag, void *stream);
+
+/* The same collective in its low-latency form (same reference interface as
+ * above): two-shot with the arrival marker in the data -- no flag exchange,
+ * no fence, no in-switch reduction.  Each rank writes slice j of its partial
+ * into rank j's reduce-scatter region (peer stores); the owner polls its
+ * region until every element has arrived, sums the ranks' values in rank
+ * order in fp32, rounds once to fp16 and multicasts the sum (multimem.st)
+ * into every rank's all-gather region, which every rank polls and copies
+ * into its data.  Sums are the fp32 rank-order sums rounded once, the same
+ * bits on every rank; NaN sums come out as the canonical NaN 0x7E00.
+ * Memory, allocated by the caller on every rank in memory bound to one NVLink
+ * multicast object: the data (num_elems fp16), a reduce-scatter and an
+ * all-gather region of 2 * region_elems fp16 each (region_elems >=
+ * num_elems, a multiple of 8), both filled with 0xFF bytes before the first
+ * call on any rank, and a zero-initialised signal area of
+ * b200kv_nvls_signal_bytes().  Arguments: this rank's data, the table of all
+ * ranks' reduce-scatter regions mapped here (rank order), this rank's
+ * all-gather region and the multicast address of the all-gather regions,
+ * region_elems, this rank's signal area.  ctas in [0, 256] (0 = 32).  Waits
+ * are bounded (2 s, then B200KV_DEVERR_TIMEOUT); after a timeout the regions
+ * may hold stale values: refill them before the next call. */
+B200KV_API int b200kv_nvls_allreduce_ll_f16(void *data, void *const *rs_regions, void *ag_region,
+                                            void *ag_multicast, int64_t region_elems, void *signal_area,
+                                            int32_t rank, int32_t world, int64_t num_elems, int32_t ctas,
+                                            int32_t *error_flag, void *stream);
 
 /* Fused o_proj GEMM + SUM all-reduce of the tensor-parallel step, one kernel
  * per rank: out[b, n] = sum over ranks of sum_k attn[b, k] * w[n, k]

@@ -5,8 +5,8 @@ Each rank runs the CUDA decode kernel on its KV-head shard and its o_proj
 partial, then the SUM all-reduce (the reference's TP collective,
 SpyreCCLBackend::allreduce, torch_spyre/csrc/distributed/spyre_ccl.cpp:470-494)
 by each path: NCCL, the peer-memory all-reduce kernel, the fused o_proj +
-all-reduce kernel, and (where the GPUs offer NVLink multicast) the NVLink
-SHARP all-reduce kernel.  Every result must match the oracle -- the
+all-reduce kernel, and (where the GPUs offer NVLink multicast) the two NVLink
+SHARP all-reduce kernels.  Every result must match the oracle -- the
 reference's CPU eager decode of all heads followed by the full o_proj in fp32
 -- within 1e-2 abs + 1e-2 rel (the decode tolerance carried through an fp16
 attention output and fp16 partials summed over K = 8192 / N products), and
@@ -72,11 +72,16 @@ def _worker(rank, world, port, results):
         ar.close()
         ys = {"nccl": y_nccl, "peer": y_peer, "fused": y_fused}
         try:  # the NVLink SHARP all-reduce, where the GPUs offer multicast
-            nv = NvlsAllReduce(128 * HIDDEN)
+            nv = NvlsAllReduce(128 * HIDDEN, low_latency=False)
         except RuntimeError:
             nv = None
         if nv is not None:
             ys["nvls"] = tp_decode_step(*args, allreduce=nv).cpu().clone()
+            torch.cuda.synchronize()
+            flag |= int(nv.error_flag.item())
+            nv.close()
+            nv = NvlsAllReduce(128 * HIDDEN, low_latency=True)
+            ys["nvls_ll"] = tp_decode_step(*args, allreduce=nv).cpu().clone()
             torch.cuda.synchronize()
             flag |= int(nv.error_flag.item())
             nv.close()

@@ -194,6 +194,7 @@ SIGNATURES = {
     "b200kv_peer_allreduce_f16": (ctypes.c_int, [_p, _i32, _i32, _i64, _i64, _i32, _p, _p]),
     "b200kv_nvls_signal_bytes": (_i64, []),
     "b200kv_nvls_allreduce_f16": (ctypes.c_int, [_p, _p, _i32, _i32, _i64, _i32, _p, _p]),
+    "b200kv_nvls_allreduce_ll_f16": (ctypes.c_int, [_p, _p, _p, _p, _i64, _p, _i32, _i32, _i64, _i32, _p, _p]),
     "b200kv_quantize_fp8_f16": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _i64, _p]),
     "b200kv_dequantize_fp8_f16": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _i64, _p]),
     "b200kv_kv_append_fp8": (

@@ -199,8 +199,13 @@ class NvlsAllReduce:
 
     The buffer is PyTorch symmetric memory (one allocation per rank, bound to
     an NVLink multicast object by ``rendezvous``): the data region first, then
-    the kernel's signal area.  PyTorch only provides that memory and its
-    mapping; the collective is this library's kernel.  Usage matches
+    (low-latency kernel only) the reduce-scatter and all-gather receive
+    regions, then the kernel's signal area.  PyTorch only provides that memory
+    and its mapping; the collective is this library's kernel.  ``low_latency``
+    picks ``b200kv_nvls_allreduce_ll_f16`` (two-shot with the arrival marker
+    in the data: peer stores, then one multicast store, no barrier) over
+    ``b200kv_nvls_allreduce_f16`` (in-switch reduction between two flag
+    barriers).  Usage matches
     :class:`PeerAllReduce`: ``buffer(shape)`` is the view a producer writes,
     ``all_reduce(view)`` sums it in place across ranks on the current stream;
     every rank makes the same calls; graph replays are supported; waits are
@@ -208,7 +213,8 @@ class NvlsAllReduce:
     the GPUs offer no multicast (``available()`` tells beforehand).
     """
 
-    def __init__(self, capacity: int, group=None, device: Optional[torch.device] = None, ctas: int = 32):
+    def __init__(self, capacity: int, group=None, device: Optional[torch.device] = None,
+                 ctas: Optional[int] = None, low_latency: bool = True):
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
 
@@ -218,13 +224,20 @@ class NvlsAllReduce:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         q = 8 * self.world
         self.capacity = -(-int(capacity) // q) * q
-        self.ctas = int(ctas)
+        self.low_latency = bool(low_latency)
+        # measured on B200 (2 MiB): the low-latency kernel gains up to 64 CTAs
+        # (N = 2: 11.3 -> 9.3 us, N = 4: 13.2 -> 11.4 us), the in-switch one does not
+        self.ctas = int(ctas) if ctas is not None else (64 if self.low_latency else 32)
         lib = _lib.lib()
         self._data_bytes = -(-self.capacity * 2 // 256) * 256
         sig = int(lib.b200kv_nvls_signal_bytes())
+        # [data | reduce-scatter x 2 | all-gather x 2 | signals] (low latency), [data | signals]
+        self._rs_off = self._data_bytes
+        self._ag_off = self._rs_off + 2 * self._data_bytes
+        self._sig_off = self._ag_off + 2 * self._data_bytes if self.low_latency else self._data_bytes
         with torch.cuda.device(self.device):
             try:
-                self._buf = symm_mem.empty(self._data_bytes + sig, dtype=torch.uint8, device=self.device)
+                self._buf = symm_mem.empty(self._sig_off + sig, dtype=torch.uint8, device=self.device)
                 self._hdl = symm_mem.rendezvous(self._buf, self.group.group_name)
                 mc = int(self._hdl.multicast_ptr)
             except Exception:  # no symmetric memory here: no multicast either
@@ -237,11 +250,17 @@ class NvlsAllReduce:
                 self._hdl = None
                 self._buf = None
                 raise RuntimeError("NVLink multicast is not available on these GPUs")
-            self._buf[self._data_bytes:].zero_()
+            # the receive regions hold the "not arrived" sentinel between
+            # calls; every rank fills its own before any rank may write them
+            if self.low_latency:
+                self._buf[self._rs_off : self._sig_off].fill_(0xFF)
+            self._buf[self._sig_off :].zero_()
             torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         self._mc = mc
-        self._signals = (ctypes.c_void_p * self.world)(*[int(p) + self._data_bytes for p in self._hdl.buffer_ptrs])
+        ptrs = [int(p) for p in self._hdl.buffer_ptrs]
+        self._signals = (ctypes.c_void_p * self.world)(*[p + self._sig_off for p in ptrs])
+        self._rs = (ctypes.c_void_p * self.world)(*[p + self._rs_off for p in ptrs])
         self._data = self._buf[: self.capacity * 2].view(torch.float16)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -269,8 +288,15 @@ class NvlsAllReduce:
         """Sums ``t`` (a view from ``buffer``) over the ranks, in place."""
         if t.dtype != torch.float16 or not t.is_contiguous() or t.data_ptr() != self._data.data_ptr():
             raise ValueError("all_reduce takes a contiguous fp16 view returned by buffer()")
-        _lib.call("b200kv_nvls_allreduce_f16", self._mc, self._signals, self.rank, self.world, t.numel(),
-                  self.ctas, self.error_flag.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if self.low_latency:
+            base = self._buf.data_ptr()
+            _lib.call("b200kv_nvls_allreduce_ll_f16", t.data_ptr(), self._rs, base + self._ag_off,
+                      self._mc + self._ag_off, self._data_bytes // 2, base + self._sig_off, self.rank, self.world,
+                      t.numel(), self.ctas, self.error_flag.data_ptr(), stream)
+        else:
+            _lib.call("b200kv_nvls_allreduce_f16", self._mc, self._signals, self.rank, self.world, t.numel(),
+                      self.ctas, self.error_flag.data_ptr(), stream)
         return t
 
     def close(self) -> None:
