@@ -607,33 +607,42 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         # cross in their own H2D copy and its output in its own D2H copy, on
         # two copy streams, while the steps' kernels run back to back.  The
         # uploads run ahead of the kernels (the whole graph's steps' inputs are
-        # staged at once), and the compute stream waits on the upload stream
-        # once per group of 4 steps (the downloads are forked once per group):
-        # a kernel that waits on a copy cannot start under its predecessor
+        # staged at once; an upload takes a fraction of a step), and the
+        # compute stream waits on the upload stream three times per graph: for
+        # step 0's inputs alone (so the first kernel does not wait on a batch
+        # of copies), then before steps 1 and 7 for the uploads up to the next
+        # wait.  The downloads are forked after kernels 6, P - 2 and P - 1, so
+        # only the last step's output crosses after the last kernel.  A kernel
+        # that waits on a copy cannot start under its predecessor
         # (programmatic dependent launch applies between kernels only), which
-        # costs ~7 us per waiting kernel on B200.
+        # costs ~7 us per waiting kernel on B200, hence few waits.
+        P = pipe_steps
+        up_groups = [(a, min(b, P)) for a, b in ((0, 1), (1, 7), (7, P)) if a < min(b, P)]
+        down_groups = [(a, b) for a, b in ((0, min(7, P - 1)), (min(7, P - 1), P - 1), (P - 1, P)) if a < b]
         cur = torch.cuda.current_stream(device)
         up_stream.wait_stream(cur)
         down_stream.wait_stream(cur)
-        landed = []
+        landed = {}
         with torch.cuda.stream(up_stream):
-            for k in range(pipe_steps):
-                staged[k][1].copy_(staged[k][0], non_blocking=True)
-                if k % group == group - 1 or k == pipe_steps - 1:
-                    ev = torch.cuda.Event()
-                    ev.record(up_stream)
-                    landed.append(ev)
+            for a, b in up_groups:
+                for k in range(a, b):
+                    staged[k][1].copy_(staged[k][0], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(up_stream)
+                landed[a] = ev
+        down_after = {b - 1: (a, b) for a, b in down_groups}
         outs = []
-        for k in range(pipe_steps):
-            if k % group == 0:
-                cur.wait_event(landed[k // group])
+        for k in range(P):
+            if k in landed:
+                cur.wait_event(landed[k])
             outs.append(compute(k))
-            if k % group == group - 1 or k == pipe_steps - 1:
+            if k in down_after:
+                a, b = down_after[k]
                 done = torch.cuda.Event()
                 done.record(cur)
                 with torch.cuda.stream(down_stream):
                     down_stream.wait_event(done)
-                    for j in range(k - k % group, k + 1):
+                    for j in range(a, b):
                         staged[j][3].copy_(outs[j], non_blocking=True)
         cur.wait_stream(up_stream)
         cur.wait_stream(down_stream)
@@ -713,7 +722,8 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
                      " + all-reduce) with pinned host buffers, one H2D copy of each step's inputs and one D2H "
                      "copy of its output, "
                      + (("captured in a CUDA graph of 16 steps and replayed; the copies run on two copy streams, "
-                         "the uploads ahead of the kernels, the compute stream waiting on them once per 4 steps")
+                         "the uploads ahead of the kernels, the compute stream waiting on them before steps 0, 1 "
+                         "and 7, the downloads forked after steps 6, 14 and 15")
                         if graph_ms is not None and not tp else
                         "captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
                         "overlapping the neighbouring steps' compute" if graph_ms is not None
