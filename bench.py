@@ -565,8 +565,8 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         return host, dev, views, h_out, data
 
     n_sets = len(sets)
-    # one staging buffer per step of a captured graph (tp70b: per input set)
-    pipe_steps = n_sets if tp else n_sets * max(1, 16 // n_sets)
+    # one staging buffer per step of a captured graph of 32 steps (tp70b: per input set)
+    pipe_steps = n_sets if tp else n_sets * max(1, 32 // n_sets)
     staged = [pack(sets[k % n_sets]) for k in range(pipe_steps)]
     B = sets[0].q.shape[0]
     h2d = int(statistics.mean(x[4] for x in staged))
@@ -611,14 +611,16 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         # compute stream waits on the upload stream three times per graph: for
         # step 0's inputs alone (so the first kernel does not wait on a batch
         # of copies), then before steps 1 and 7 for the uploads up to the next
-        # wait.  The downloads are forked after kernels 6, P - 2 and P - 1, so
-        # only the last step's output crosses after the last kernel.  A kernel
+        # wait.  The downloads are forked after kernels 6, 14, 22, ..., P - 2
+        # and P - 1, so only the last step's output crosses after the last
+        # kernel.  A kernel
         # that waits on a copy cannot start under its predecessor
         # (programmatic dependent launch applies between kernels only), which
         # costs ~7 us per waiting kernel on B200, hence few waits.
         P = pipe_steps
         up_groups = [(a, min(b, P)) for a, b in ((0, 1), (1, 7), (7, P)) if a < min(b, P)]
-        down_groups = [(a, b) for a, b in ((0, min(7, P - 1)), (min(7, P - 1), P - 1), (P - 1, P)) if a < b]
+        bounds = [0, *range(7, P - 1, 8), P - 1, P]
+        down_groups = [(a, b) for a, b in zip(bounds, bounds[1:]) if a < b]
         cur = torch.cuda.current_stream(device)
         up_stream.wait_stream(cur)
         down_stream.wait_stream(cur)
@@ -721,9 +723,9 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
             "path": ("torch.ops.b200kv.decode_attention_append (tp70b: kv_append + decode_attention + o_proj"
                      " + all-reduce) with pinned host buffers, one H2D copy of each step's inputs and one D2H "
                      "copy of its output, "
-                     + (("captured in a CUDA graph of 16 steps and replayed; the copies run on two copy streams, "
+                     + (("captured in a CUDA graph of 32 steps and replayed; the copies run on two copy streams, "
                          "the uploads ahead of the kernels, the compute stream waiting on them before steps 0, 1 "
-                         "and 7, the downloads forked after steps 6, 14 and 15")
+                         "and 7, the downloads forked after steps 6, 14, 22, 30 and 31")
                         if graph_ms is not None and not tp else
                         "captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
                         "overlapping the neighbouring steps' compute" if graph_ms is not None
