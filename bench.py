@@ -81,6 +81,11 @@ def parse_args():
     return p.parse_args()
 
 
+# decode steps per captured CUDA graph (the headline loop) and per captured
+# e2e pipeline graph: a graph replay starts without programmatic early start
+# and, in the e2e pipeline, with an upload wait and ends with a download
+GRAPH_STEPS = 32
+E2E_GRAPH_STEPS = 64
 DEFAULT_STEPS = {"gqa_b16": 20000, "mha_b1": 20000, "gqa_long": 4000, "tp70b": 2000, "relayout": 2000}
 
 
@@ -265,7 +270,7 @@ def workload_config(args, cfg, rank, world):
                             else f"one rank's share of tp{split} (no all-reduce)" if tp
                             else f"dp{world} (sequence shards)"),
             "l2": f"{n_sets} rotating input sets, {kv / 1e6:.1f} MB KV read per step (L2 126 MB)",
-            "graphs": (f"up to {max(1, 16 // n_sets) * n_sets} steps per graph replay" if graphed
+            "graphs": (f"up to {max(1, GRAPH_STEPS // n_sets) * n_sets} steps per graph replay" if graphed
                        else "eager (NCCL step)"),
             "decode_launch": ("B200KV_DECODE_INPUTS_READY (inputs written before the previous step)"
                               if args.kv_dtype == "fp16" and not args.no_early_start else "default")}
@@ -379,10 +384,10 @@ def run_ours(args, rank, world, local):
 
     # Steps replay from CUDA graphs, as a serving loop replays its captured
     # decode steps: one graph holding `rounds` passes over the rotating input
-    # sets (up to 16 steps back to back with no graph launch in between), one
+    # sets (up to GRAPH_STEPS steps back to back with no graph launch in between), one
     # holding one pass, and one single-step graph per set for a remainder.
     graphed = not (tp and world > 1) or args.nccl_graph or ar is not None
-    rounds = max(1, 16 // n_sets)
+    rounds = max(1, GRAPH_STEPS // n_sets)
     with torch.cuda.stream(stream):
         for s in sets:  # warm the op once per set before capture
             step(s)
@@ -565,8 +570,8 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         return host, dev, views, h_out, data
 
     n_sets = len(sets)
-    # one staging buffer per step of a captured graph of 32 steps (tp70b: per input set)
-    pipe_steps = n_sets if tp else n_sets * max(1, 32 // n_sets)
+    # one staging buffer per step of a captured graph (tp70b: per input set)
+    pipe_steps = n_sets if tp else n_sets * max(1, E2E_GRAPH_STEPS // n_sets)
     staged = [pack(sets[k % n_sets]) for k in range(pipe_steps)]
     B = sets[0].q.shape[0]
     h2d = int(statistics.mean(x[4] for x in staged))
@@ -608,17 +613,18 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         # two copy streams, while the steps' kernels run back to back.  The
         # uploads run ahead of the kernels (the whole graph's steps' inputs are
         # staged at once; an upload takes a fraction of a step), and the
-        # compute stream waits on the upload stream three times per graph: for
+        # compute stream waits on the upload stream a few times per graph: for
         # step 0's inputs alone (so the first kernel does not wait on a batch
-        # of copies), then before steps 1 and 7 for the uploads up to the next
-        # wait.  The downloads are forked after kernels 6, 14, 22, ..., P - 2
+        # of copies), then before steps 1, 7 and 31, 63, ... for the uploads
+        # up to the next wait.  The downloads are forked after kernels 6, 14, 22, ..., P - 2
         # and P - 1, so only the last step's output crosses after the last
         # kernel.  A kernel
         # that waits on a copy cannot start under its predecessor
         # (programmatic dependent launch applies between kernels only), which
         # costs ~7 us per waiting kernel on B200, hence few waits.
         P = pipe_steps
-        up_groups = [(a, min(b, P)) for a, b in ((0, 1), (1, 7), (7, P)) if a < min(b, P)]
+        ubounds = sorted({min(x, P) for x in (0, 1, 7, *range(31, P - 1, 32), P)})
+        up_groups = [(a, b) for a, b in zip(ubounds, ubounds[1:]) if a < b]
         bounds = [0, *range(7, P - 1, 8), P - 1, P]
         down_groups = [(a, b) for a, b in zip(bounds, bounds[1:]) if a < b]
         cur = torch.cuda.current_stream(device)
@@ -723,9 +729,9 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
             "path": ("torch.ops.b200kv.decode_attention_append (tp70b: kv_append + decode_attention + o_proj"
                      " + all-reduce) with pinned host buffers, one H2D copy of each step's inputs and one D2H "
                      "copy of its output, "
-                     + (("captured in a CUDA graph of 32 steps and replayed; the copies run on two copy streams, "
-                         "the uploads ahead of the kernels, the compute stream waiting on them before steps 0, 1 "
-                         "and 7, the downloads forked after steps 6, 14, 22, 30 and 31")
+                     + (("captured in a CUDA graph of 64 steps and replayed; the copies run on two copy streams, "
+                         "the uploads ahead of the kernels, the compute stream waiting on them before steps 0, 1, "
+                         "7 and 31, the downloads forked after step 6, every 8 steps after it and the last two")
                         if graph_ms is not None and not tp else
                         "captured once in a CUDA graph and replayed, uploads / downloads on copy streams "
                         "overlapping the neighbouring steps' compute" if graph_ms is not None
