@@ -273,7 +273,7 @@ def workload_config(args, cfg, rank, world):
             "graphs": (f"up to {max(1, GRAPH_STEPS // n_sets) * n_sets} steps per graph replay" if graphed
                        else "eager (NCCL step)"),
             "decode_launch": ("B200KV_DECODE_INPUTS_READY (inputs written before the previous step)"
-                              if args.kv_dtype == "fp16" and not args.no_early_start else "default")}
+                              if not args.no_early_start else "default")}
 
 
 def profile_key(args) -> str:
@@ -361,13 +361,13 @@ def run_ours(args, rank, world, local):
             return tp_decode_step(shard, s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, w_o,
                                   out=partial if ar is None or fused else None, k_scale=s.k_scale,
                                   v_scale=s.v_scale, allreduce=ar, fused_oproj=fused,
-                                  inputs_ready=not fp8 and not args.no_early_start)
+                                  inputs_ready=not args.no_early_start)
         return decode_only(s)
 
     # The steps' pools, block tables and context lengths are written once,
     # before any step: each decode may plan and start its page loads while the
-    # previous step's kernel finishes (B200KV_DECODE_INPUTS_READY; fp16 pages).
-    ready = not fp8 and not tp and not args.no_early_start
+    # previous step's kernel finishes (B200KV_DECODE_INPUTS_READY).
+    ready = not tp and not args.no_early_start
 
     def decode_only(s):
         return tsb.decode_attention(s.q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,

@@ -374,6 +374,23 @@ B200KV_API int b200kv_decode_attention_fp8(
     void *workspace, int64_t workspace_bytes, int32_t *error_flag,
     void *stream);
 
+/* b200kv_decode_attention_fp8 with launch flags (the same interface as
+ * above; flags as b200kv_decode_attention_ex_f16): B200KV_DECODE_INPUTS_READY
+ * lets the kernel plan and start its page loads before the preceding kernel
+ * on the stream finishes; the pools, block table and context lengths must
+ * then have been written before that kernel began (q and the scales may be
+ * written by it).  Same result either way. */
+B200KV_API int b200kv_decode_attention_ex_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool,
+    const void *v_pool, const void *k_scale, const void *v_scale,
+    const int32_t *block_table, int64_t block_table_stride,
+    const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads,
+    int64_t num_kv_heads, int64_t head_dim, int64_t num_blocks,
+    int64_t max_blocks_per_seq, float scale, int64_t num_splits,
+    void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    uint32_t flags, void *stream);
+
 /* Fused append + decode over fp8 pools: as
  * b200kv_decode_attention_append_f16, the new fp16 rows quantized into the
  * pools (as b200kv_kv_append_fp8) and used, quantized, for this step. */

@@ -220,3 +220,41 @@ def test_early_start_gives_the_same_bits(name, hkv):
     first = opa.decode_attention_cpu(sets[0].q, sets[0].k_pool, sets[0].v_pool, sets[0].block_table,
                                      sets[0].context_lens)
     torch.testing.assert_close(got[0].cpu().float(), first.float(), atol=2e-3, rtol=1e-2)
+
+
+@pytest.mark.parametrize("name", ["gqa_b16", "tp70b"])
+def test_early_start_gives_the_same_bits_fp8(name):
+    """The early start over e4m3 pools (b200kv_decode_attention_ex_fp8):
+    chained decodes whose q is the previous output, eager and graph-replayed,
+    give the same bits as the default launch."""
+    from torch_spyre_b200.workloads import quantize_decode_inputs
+
+    cfg = DECODE_CONFIGS[name]
+    kw = {"num_kv_heads": 1} if name == "tp70b" else {}
+    sets = [quantize_decode_inputs(make_decode_inputs(cfg, device="cuda", seed_tag=f"early8-{i}", **kw))
+            for i in range(2)]
+
+    def chain(ready):
+        outs, q = [], sets[0].q
+        for i in range(6):
+            s = sets[i % 2]
+            q = tsb.decode_attention(q, s.k_pool, s.v_pool, s.block_table, s.context_lens, k_scale=s.k_scale,
+                                     v_scale=s.v_scale, inputs_ready=ready)
+            outs.append(q)
+        return outs
+
+    ref = chain(False)
+    got = chain(True)
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        chain(True)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            graphed = chain(True)
+        g.replay()
+    stream.synchronize()
+    for a, b in zip(ref, graphed):
+        assert torch.equal(a, b)

@@ -217,6 +217,22 @@ SIGNATURES = {
             _p, _p,  # error_flag, stream
         ],
     ),
+    "b200kv_decode_attention_ex_fp8": (
+        ctypes.c_int,
+        [
+            _p, _i64, _i64,  # q, q_stride_b, q_stride_h
+            _p, _p, _p, _p,  # k_pool, v_pool, k_scale, v_scale
+            _p, _i64,  # block_table, block_table_stride
+            _p,  # context_lens
+            _p, _i64, _i64,  # out, out_stride_b, out_stride_h
+            _p,  # lse
+            _i64, _i64, _i64, _i64,  # batch, Hq, Hkv, head_dim
+            _i64, _i64,  # num_blocks, max_blocks_per_seq
+            _f32, _i64,  # scale, num_splits
+            _p, _i64,  # workspace, workspace_bytes
+            _p, ctypes.c_uint32, _p,  # error_flag, flags, stream
+        ],
+    ),
     "b200kv_decode_attention_append_fp8": (
         ctypes.c_int,
         [

@@ -256,6 +256,23 @@ extern "C" int b200kv_decode_attention_fp8(
                       true, k_scale, v_scale);
 }
 
+extern "C" int b200kv_decode_attention_ex_fp8(
+    const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_pool, const void *v_pool,
+    const void *k_scale, const void *v_scale, const int32_t *block_table,
+    int64_t block_table_stride, const int32_t *context_lens, void *out, int64_t out_stride_b,
+    int64_t out_stride_h, float *lse, int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_dim, int64_t num_blocks, int64_t max_blocks_per_seq, float scale,
+    int64_t num_splits, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+    uint32_t flags, void *stream) {
+  if (flags & ~uint32_t(B200KV_DECODE_INPUTS_READY))
+    return set_error(B200KV_ERR_INVALID_ARG, "unknown flags 0x%x", flags);
+  return decode_entry(q, q_stride_b, q_stride_h, k_pool, v_pool, block_table, block_table_stride,
+                      context_lens, out, out_stride_b, out_stride_h, lse, batch, num_q_heads,
+                      num_kv_heads, head_dim, num_blocks, max_blocks_per_seq, scale, num_splits,
+                      workspace, workspace_bytes, error_flag, stream, nullptr, nullptr, 0, 0, false,
+                      true, k_scale, v_scale, nullptr, 0, flags);
+}
+
 extern "C" int b200kv_decode_attention_append_fp8(
     const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_new, const void *v_new,
     int64_t new_stride_b, int64_t new_stride_h, void *k_pool, void *v_pool, const void *k_scale,

@@ -24,7 +24,8 @@ import torch
 
 from . import _lib
 from .layout import PAGE_TOKENS
-from .ops import _check_rope_freqs, _maybe_check_flag, _ptr, _require_cuda, _stream_ptr, workspace_for
+from .ops import (DECODE_INPUTS_READY, _check_rope_freqs, _maybe_check_flag, _ptr, _require_cuda, _stream_ptr,
+                  workspace_for)
 
 FP8 = torch.float8_e4m3fn
 FP8_E4M3_MAX = 448.0
@@ -202,6 +203,7 @@ def _decode_attention_fp8_op(
     scale: float,
     num_splits: int,
     error_flag: Optional[torch.Tensor],
+    inputs_ready: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     _require_cuda(q, k_pool, v_pool, k_scale, v_scale, block_table, context_lens)
     _check_pool8(k_pool, "k_pool")
@@ -219,8 +221,7 @@ def _decode_attention_fp8_op(
         return out, lse
     wbytes = _lib.lib().b200kv_decode_workspace_bytes(B, Hq, Hkv, D)
     ws = workspace_for(q.device, wbytes) if wbytes > 0 else torch.empty(0, dtype=torch.uint8, device=q.device)
-    _lib.call(
-        "b200kv_decode_attention_fp8",
+    args = (
         q.data_ptr(), q.stride(0), q.stride(1),
         k_pool.data_ptr(), v_pool.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
         block_table.data_ptr(), block_table.stride(0),
@@ -230,14 +231,19 @@ def _decode_attention_fp8_op(
         B, Hq, Hkv, D, NB, block_table.shape[1],
         float(scale), int(num_splits),
         ws.data_ptr(), ws.numel(),
-        _ptr(error_flag), _stream_ptr(q.device),
+        _ptr(error_flag),
     )
+    if inputs_ready:
+        _lib.call("b200kv_decode_attention_ex_fp8", *args, DECODE_INPUTS_READY, _stream_ptr(q.device))
+    else:
+        _lib.call("b200kv_decode_attention_fp8", *args, _stream_ptr(q.device))
     _maybe_check_flag(error_flag, "decode_attention_fp8")
     return out, lse
 
 
 @_decode_attention_fp8_op.register_fake
-def _(q, k_pool, v_pool, k_scale, v_scale, block_table, context_lens, scale, num_splits, error_flag):
+def _(q, k_pool, v_pool, k_scale, v_scale, block_table, context_lens, scale, num_splits, error_flag,
+      inputs_ready=False):
     B, Hq, D = q.shape
     return q.new_empty((B, Hq, D)), q.new_empty((B, Hq), dtype=torch.float32)
 

@@ -193,10 +193,11 @@ def decode_attention(
     [B, max_blocks]; context_lens int32 [B].  Returns out [B, Hq, D] fp16 (and
     the natural-log LSE [B, Hq] fp32 when ``return_lse``).
 
-    ``inputs_ready`` (fp16 pools): the pools, block table and context lengths
-    were written before the preceding kernel on the stream began (q may be
-    written by it), so the kernel may plan and start its page loads while that
-    kernel finishes (B200KV_DECODE_INPUTS_READY).  Same result either way.
+    ``inputs_ready`` (fp16 or fp8 pools): the pools, block table and context
+    lengths were written before the preceding kernel on the stream began (q
+    and the fp8 scales may be written by it), so the kernel may plan and start
+    its page loads while that kernel finishes (B200KV_DECODE_INPUTS_READY).
+    Same result either way.
     """
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
@@ -204,7 +205,7 @@ def decode_attention(
         from . import fp8  # noqa: F401  (registers the fp8 ops)
         out, lse = torch.ops.b200kv.decode_attention_fp8(
             q, k_pool, v_pool, _need(k_scale, "k_scale"), _need(v_scale, "v_scale"), block_table, context_lens,
-            float(scale), int(num_splits), error_flag
+            float(scale), int(num_splits), error_flag, bool(inputs_ready)
         )
     else:
         out, lse = torch.ops.b200kv.decode_attention(
