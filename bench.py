@@ -528,6 +528,19 @@ def run_ours(args, rank, world, local):
         ar.close()
 
 
+def pipeline_groups(P):
+    """Copy groups of a P-step e2e pipeline graph, as (first, end) step ranges.
+
+    Uploads: step 0 alone (the first kernel waits for its own inputs only),
+    then steps 1-6, 7-30, 31-62, ... (the compute stream waits once per group,
+    before the group's first step).  Downloads: steps 0-6, then every 8 steps,
+    then the last step alone (forked after the group's last kernel), so one
+    download is left after the last kernel."""
+    ub = sorted({min(x, P) for x in (0, 1, 7, *range(31, P - 1, 32), P)})
+    db = [0, *range(7, P - 1, 8), P - 1, P]
+    return ([(a, b) for a, b in zip(ub, ub[1:]) if a < b], [(a, b) for a, b in zip(db, db[1:]) if a < b])
+
+
 def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fused=False, early=False):
     """Public-API decode step with host buffers: H2D inputs, append, decode, D2H.
 
@@ -623,10 +636,7 @@ def run_e2e(tsb, cfg, sets, steps, warmup, stream, world, tp, w_o, ar=None, fuse
         # (programmatic dependent launch applies between kernels only), which
         # costs ~7 us per waiting kernel on B200, hence few waits.
         P = pipe_steps
-        ubounds = sorted({min(x, P) for x in (0, 1, 7, *range(31, P - 1, 32), P)})
-        up_groups = [(a, b) for a, b in zip(ubounds, ubounds[1:]) if a < b]
-        bounds = [0, *range(7, P - 1, 8), P - 1, P]
-        down_groups = [(a, b) for a, b in zip(bounds, bounds[1:]) if a < b]
+        up_groups, down_groups = pipeline_groups(P)
         cur = torch.cuda.current_stream(device)
         up_stream.wait_stream(cur)
         down_stream.wait_stream(cur)
