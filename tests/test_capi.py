@@ -107,3 +107,39 @@ def test_peer_allreduce_host_checks():
     bad = (ctypes.c_void_p * 2)(1 << 20, (1 << 21) + 16)
     assert lib.b200kv_peer_allreduce_f16(bad, 0, 2, 16, 32, 0, None, None) == 1
     assert "aligned" in _lib.last_error()
+
+
+def test_ex_entries_reject_unknown_flags():
+    lib = _lib.lib()
+    base = [1 << 20, 4096, 128, 1 << 21, 1 << 22, 1 << 23, 4, 1 << 24, 1 << 25, 4096, 128, None, 2, 32, 8, 128,
+            10, 4, 0.088, 0, None, 0, None]
+    assert lib.b200kv_decode_attention_ex_f16(*base, 2, None) == 1
+    assert "unknown flags" in _lib.last_error()
+    fp8 = base[:5] + [1 << 26, 1 << 27] + base[5:]  # k_scale, v_scale after the pools
+    assert lib.b200kv_decode_attention_ex_fp8(*fp8, 6, None) == 1
+    assert "unknown flags" in _lib.last_error()
+
+
+def test_nvls_allreduce_host_checks():
+    lib = _lib.lib()
+    assert lib.b200kv_nvls_signal_bytes() >= (64 + 2 * 256 * 8) * 4
+    rs = (ctypes.c_void_p * 2)(1 << 20, 1 << 21)
+    sig = (ctypes.c_void_p * 2)(1 << 24, 1 << 25)
+
+    def ll(data=1 << 22, ag=1 << 23, ag_mc=1 << 26, region=1024, signal=1 << 24, rank=0, world=2, n=512,
+           ctas=0, table=rs):
+        return lib.b200kv_nvls_allreduce_ll_f16(data, table, ag, ag_mc, region, signal, rank, world, n, ctas,
+                                                None, None)
+
+    assert ll(n=0) == 0                                   # nothing to do, nothing launched
+    for kw, msg in [(dict(world=9), "world"), (dict(rank=2), "rank"), (dict(n=24), "multiple of 8 * world"),
+                    (dict(region=256), "region_elems"), (dict(region=1020), "region_elems"),
+                    (dict(ctas=257), "ctas"), (dict(data=None), "aligned"), (dict(ag_mc=(1 << 26) + 8), "aligned"),
+                    (dict(table=(ctypes.c_void_p * 2)(1 << 20, None)), "reduce-scatter region")]:
+        assert ll(**kw) == 1, kw
+        assert msg in _lib.last_error(), (kw, _lib.last_error())
+    # the in-switch form: the same limits on world, size and CTAs
+    assert lib.b200kv_nvls_allreduce_f16(1 << 26, sig, 0, 2, 24, 32, None, None) == 1
+    assert lib.b200kv_nvls_allreduce_f16(1 << 26, sig, 0, 2, 512, 257, None, None) == 1
+    assert "ctas" in _lib.last_error()
+    assert lib.b200kv_nvls_allreduce_f16(1 << 26, sig, 0, 2, 0, 32, None, None) == 0
